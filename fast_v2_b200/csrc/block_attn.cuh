@@ -1,0 +1,480 @@
+// (d) Block attention over the KV cache on sm_100a: TMA -> shared memory,
+// tcgen05.mma (bf16 in, fp32 accumulate in TMEM), online softmax in
+// registers, GQA packed into the MMA M dimension.
+//
+// One CTA = (batch row b, KV head g, query chunk, KV split).  The G = Hq/Hkv
+// query heads that share KV head g, times the qc queries of the chunk, form
+// R = G*qc <= 256 rows (224 for the 7B geometry: 7 heads x 32 queries),
+// processed as one or two 128-row MMA tiles against the same K/V tiles -- the
+// GQA expansion never touches memory.  Keys stream in tiles of 64 through a
+// 3-stage TMA pipeline.
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer (Q once, then K/V tiles)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  softmax for rows   0..127 (TMEM lanes = rows)
+//   warps 6..9  softmax for rows 128..255
+// Per tile j and row tile m:  S_m = Q_m K_j^T  (TMEM, 64 fp32 columns)  ->
+// softmax warps load S, mask, update the running max (O in TMEM is rescaled
+// only when the max grows by more than 2^8, otherwise the stale max is kept:
+// the result is identical up to rounding), write P = exp2(S - max) as bf16
+// into a 128B-swizzled shared tile  ->  O_m += P V_j  (TMEM, 128 columns).
+// S_m(j+1) is issued as soon as S_m(j) has been read, so the tensor core
+// overlaps the softmax of the current tile.
+//
+// TMEM columns: S_0 [0,64) S_1 [64,128) O_0 [128,256) O_1 [256,384).
+// Shared memory: Q 64 KB | K 3x16 KB | V 3x16 KB | P 2x16 KB | barriers.
+#pragma once
+#include <cuda.h>
+#include "sm100_ptx.cuh"
+
+namespace fdl {
+
+constexpr int kAttnThreads = 320;
+constexpr int kBlockN = 64;
+constexpr int kStages = 3;
+constexpr int kHeadDim = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;
+constexpr uint32_t kTmemO = 128;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
+
+constexpr uint32_t kSmemQ = 0;                        // 2 halves x 256 rows x 128 B
+constexpr uint32_t kQHalf = 256 * 128;                // 32 KB
+constexpr uint32_t kSmemK = 2 * kQHalf;               // 65536
+constexpr uint32_t kKVHalf = kBlockN * 128;           // 8 KB (64 keys x 64 dims)
+constexpr uint32_t kKVTile = 2 * kKVHalf;             // 16 KB
+constexpr uint32_t kSmemV = kSmemK + kStages * kKVTile;
+constexpr uint32_t kSmemP = kSmemV + kStages * kKVTile;
+constexpr uint32_t kPTile = 128 * 128;                // 128 rows x 64 keys bf16
+constexpr uint32_t kSmemBar = kSmemP + 2 * kPTile;    // 196608
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignment slack
+
+struct AttnParams {
+  CUtensorMap tm_q;   // dims (D, Hq, Sq, B), box (64, G, qc, 1)
+  CUtensorMap tm_k;   // dims (D, Hkv, cap, B), box (64, 1, 64, 1); (D, cap, Hkv, B) if head-major
+  CUtensorMap tm_v;
+  CUtensorMap tm_kb;  // dims (D, Hkv, n_blk, B), box (64, 1, 64, 1)
+  CUtensorMap tm_vb;
+  const int32_t* seqlens;
+  const int32_t* q_pos;
+  __nv_bfloat16* out;
+  float* ws_o;
+  float* ws_lse;
+  int B, Sq, Hq, Hkv, G, qc, n_qchunks, cap, n_blk, mask_block, splits, n_mt;
+  int kv_hmajor, blk_hmajor;  // 1: map dims are (D, S, H, B) (head-major memory)
+  float scale_log2;
+  int64_t o_sb, o_ss, o_sh;  // elements
+};
+
+struct AttnBarriers {
+  uint64_t q_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t s_empty[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint64_t fin;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(AttnBarriers) <= 256, "barrier block");
+
+struct TileInfo {
+  int src;    // 0 = cache, 1 = appended block
+  int key0;   // first key within its source
+  int valid;  // valid keys in this tile
+  int kpos0;  // absolute position of key0
+};
+
+__device__ __forceinline__ TileInfo tile_info(int i, int n1, int len, int n_blk) {
+  TileInfo t;
+  if (i < n1) {
+    t.src = 0;
+    t.key0 = i * kBlockN;
+    t.valid = min(kBlockN, len - t.key0);
+    t.kpos0 = t.key0;
+  } else {
+    t.src = 1;
+    t.key0 = (i - n1) * kBlockN;
+    t.valid = min(kBlockN, n_blk - t.key0);
+    t.kpos0 = len + t.key0;
+  }
+  return t;
+}
+
+// Wait without honouring the abort flag (used only to drain in-flight work).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = ptx::globaltimer();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (ptx::globaltimer() - t0 > kWaitTimeoutNs) break;
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  AttnBarriers* bars = reinterpret_cast<AttnBarriers*>(smem + kSmemBar);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int g = blockIdx.y % p.Hkv;
+  const int qch = blockIdx.y / p.Hkv;
+  const int split = blockIdx.x;
+  const int q0 = qch * p.qc;
+  const int R = p.G * p.qc;
+
+  int len = p.seqlens[b];
+  if (len < 0 || len > p.cap) {
+    if (threadIdx.x == 0 && g == 0 && qch == 0 && split == 0) report(FDL_DEV_LENGTH, len);
+    len = len < 0 ? 0 : p.cap;
+  }
+  const int n1 = (len + kBlockN - 1) / kBlockN;
+  const int n2 = p.n_blk > 0 ? (p.n_blk + kBlockN - 1) / kBlockN : 0;
+  const int n_all = n1 + n2;
+  const int per = (n_all + p.splits - 1) / p.splits;
+  const int t_beg = min(n_all, split * per);
+  const int T = min(n_all, t_beg + per) - t_beg;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&bars->kv_full[s], 1);
+      ptx::mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int m = 0; m < 2; ++m) {
+      ptx::mbar_init(&bars->s_full[m], 1);
+      ptx::mbar_init(&bars->s_empty[m], 4);
+      ptx::mbar_init(&bars->p_full[m], 4);
+      ptx::mbar_init(&bars->pv_done[m], 1);
+    }
+    ptx::mbar_init(&bars->fin, 1);
+    bars->abort = 0;
+    ptx::fence_mbar_init();
+  }
+  // Rows of the last MMA tile beyond R are padding: zero them so the padded
+  // MMA rows compute on finite data.
+  {
+    const int pad0 = R, pad1 = p.n_mt * 128;
+    const int n16 = (pad1 - pad0) * 8;  // 16-byte chunks per half
+    for (int i = threadIdx.x; i < 2 * n16; i += kAttnThreads) {
+      const int half = i / n16, k = i - half * n16;
+      *reinterpret_cast<uint4*>(smem + kSmemQ + half * kQHalf + pad0 * 128 + k * 16) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (warp == 1) {
+    __syncwarp();  // .sync.aligned: the whole warp, converged
+    ptx::tmem_alloc(&bars->tmem_base, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer
+    if (lane == 0 && T > 0) {
+      ptx::prefetch_tmap(&p.tm_q);
+      ptx::prefetch_tmap(&p.tm_k);
+      ptx::prefetch_tmap(&p.tm_v);
+      const uint32_t qbytes = static_cast<uint32_t>(R) * 128u;
+      ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * qbytes);
+      ptx::tma_load_4d(smem + kSmemQ, &p.tm_q, &bars->q_full, 0, g * p.G, q0, b);
+      ptx::tma_load_4d(smem + kSmemQ + kQHalf, &p.tm_q, &bars->q_full, 64, g * p.G, q0, b);
+      int issued = 0;
+      for (int j = 0; j < T; ++j) {
+        const int st = j % kStages;
+        if (j >= kStages) {
+          if (!ptx::mbar_wait(&bars->kv_empty[st], ((j / kStages) - 1) & 1, abort, kWaitTimeoutNs, 1)) break;
+        }
+        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+        const CUtensorMap* tk = ti.src ? &p.tm_kb : &p.tm_k;
+        const CUtensorMap* tv = ti.src ? &p.tm_vb : &p.tm_v;
+        const bool hm = ti.src ? p.blk_hmajor : p.kv_hmajor;
+        const int c1 = hm ? ti.key0 : g, c2 = hm ? g : ti.key0;
+        uint8_t* ks = smem + kSmemK + st * kKVTile;
+        uint8_t* vs = smem + kSmemV + st * kKVTile;
+        ptx::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kKVTile);
+        ptx::tma_load_4d(ks, tk, &bars->kv_full[st], 0, c1, c2, b);
+        ptx::tma_load_4d(ks + kKVHalf, tk, &bars->kv_full[st], 64, c1, c2, b);
+        ptx::tma_load_4d(vs, tv, &bars->kv_full[st], 0, c1, c2, b);
+        ptx::tma_load_4d(vs + kKVHalf, tv, &bars->kv_full[st], 64, c1, c2, b);
+        issued = j + 1;
+      }
+      if (*abort) {
+        // Let every copy already in flight land before the CTA exits.
+        drain_wait(&bars->q_full, 0);
+        for (int j = max(0, issued - kStages); j < issued; ++j)
+          drain_wait(&bars->kv_full[j % kStages], (j / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && T > 0) {
+      const uint32_t idesc_s = ptx::idesc_bf16_f32(128, kBlockN, false);
+      const uint32_t idesc_o = ptx::idesc_bf16_f32(128, kHeadDim, true);
+      const uint32_t q_base = ptx::smem_u32(smem + kSmemQ);
+      const uint32_t k_base = ptx::smem_u32(smem + kSmemK);
+      const uint32_t v_base = ptx::smem_u32(smem + kSmemV);
+      const uint32_t p_base = ptx::smem_u32(smem + kSmemP);
+      bool issued_any = false;
+      // S_m(st) = Q_m * K_st^T : 8 MMAs of K = 16 over the 128 head dims.
+      auto issue_s = [&](int m, int st) {
+        const uint32_t d = tmem + kTmemS + m * kBlockN;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk & 3) * 32;  // K=16 slice inside the 128-byte swizzle row
+          const uint64_t a = ptx::smem_desc_sw128(q_base + (kk >> 2) * kQHalf + m * 128 * 128 + off, 16, 1024);
+          const uint64_t bd = ptx::smem_desc_sw128(k_base + st * kKVTile + (kk >> 2) * kKVHalf + off, 16, 1024);
+          ptx::mma_bf16_ss(d, a, bd, idesc_s, kk > 0);
+        }
+      };
+      // O_m += P_m * V_st : 4 MMAs of K = 16 over the 64 keys; V is MN-major
+      // (head dim contiguous): LBO = distance between the two 64-dim halves,
+      // SBO = 8 keys x 128 B.
+      auto issue_pv = [&](int m, int st, bool acc) {
+        const uint32_t d = tmem + kTmemO + m * kHeadDim;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t a = ptx::smem_desc_sw128(p_base + m * kPTile + kk * 32, 16, 1024);
+          const uint64_t bd = ptx::smem_desc_sw128(v_base + st * kKVTile + kk * 16 * 128, kKVHalf, 1024);
+          ptx::mma_bf16_ss(d, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = ptx::mbar_wait(&bars->q_full, 0, abort, kWaitTimeoutNs, 2) &&
+                ptx::mbar_wait(&bars->kv_full[0], 0, abort, kWaitTimeoutNs, 3);
+      if (ok) {
+        ptx::tc_fence_after();
+        for (int m = 0; m < p.n_mt; ++m) {
+          issue_s(m, 0);
+          ptx::mma_commit(&bars->s_full[m]);
+        }
+        issued_any = true;
+      }
+      for (int j = 0; ok && j < T; ++j) {
+        const int st = j % kStages;
+        const bool nxt = j + 1 < T;
+        if (nxt) {
+          ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort, kWaitTimeoutNs, 4);
+          if (!ok) break;
+        }
+        for (int m = 0; ok && m < p.n_mt; ++m) {
+          if (nxt) {
+            ok = ptx::mbar_wait(&bars->s_empty[m], j & 1, abort, kWaitTimeoutNs, 5);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            issue_s(m, (j + 1) % kStages);
+            ptx::mma_commit(&bars->s_full[m]);
+          }
+          ok = ptx::mbar_wait(&bars->p_full[m], j & 1, abort, kWaitTimeoutNs, 6);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          issue_pv(m, st, j > 0);
+          ptx::mma_commit(&bars->pv_done[m]);
+        }
+        // Only stages the producer will refill get a release; no asynchronous
+        // arrive may still be pending when the CTA exits.
+        if (j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
+      }
+      if (issued_any && !ok) {
+        ptx::mma_commit(&bars->fin);
+        drain_wait(&bars->fin, 0);
+      }
+    }
+  } else if ((warp - 2) / 4 < p.n_mt) {
+    // ------------------------------------------------------- softmax
+    const int m = (warp - 2) >> 2;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const int r = m * 128 + row;
+    const int sq_i = r / p.G;
+    const int q = q0 + sq_i;
+    const int head = g * p.G + (r - sq_i * p.G);
+    const bool valid_row = (r < R) && (q < p.Sq);
+    int qblk = 0;
+    if (p.mask_block > 0 && valid_row) {
+      const int qpos = p.q_pos ? p.q_pos[static_cast<int64_t>(b) * p.Sq + q] : len + q;
+      qblk = qpos / p.mask_block;
+    }
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + kTmemS + m * kBlockN;
+    const uint32_t t_o = tmem + lane_off + kTmemO + m * kHeadDim;
+    uint8_t* prow = smem + kSmemP + m * kPTile + (row >> 3) * 1024 + (row & 7) * 128;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < T; ++j) {
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], j & 1, abort, kWaitTimeoutNs, 7));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      float s[64];
+      ptx::tmem_ld32(t_s, *reinterpret_cast<float(*)[32]>(&s[0]));
+      ptx::tmem_ld32(t_s + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+      ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->s_empty[m]);
+
+      const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        bool allowed = valid_row && c < ti.valid;
+        if (p.mask_block > 0) allowed = allowed && (qblk >= (ti.kpos0 + c) / p.mask_block);
+        s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
+        tmax = fmaxf(tmax, s[c]);
+      }
+      const float m_new = fmaxf(m_used, tmax);
+      const bool grow = m_new > m_used + 8.f;  // true on the first finite max
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[m], (j - 1) & 1, abort, kWaitTimeoutNs, 8));
+        if (!ok) break;
+        ptx::tc_fence_after();
+      }
+      const bool rescale = grow && (m_used != -INFINITY) && j > 0;
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float alpha = rescale ? ptx::ex2(m_used - m_new) : 1.f;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          float o[32];
+          ptx::tmem_ld32(t_o + ch * 32, o);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          ptx::tmem_st32(t_o + ch * 32, o);
+        }
+        ptx::tmem_wait_st();
+      }
+      if (grow) {
+        l = (m_used == -INFINITY) ? 0.f : l * ptx::ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      float rsum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = s[c8 * 8 + 2 * e], x1 = s[c8 * 8 + 2 * e + 1];
+          const float p0 = (x0 == -INFINITY) ? 0.f : ptx::ex2(x0 - m_used);
+          const float p1 = (x1 == -INFINITY) ? 0.f : ptx::ex2(x1 - m_used);
+          const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+          rsum += __low2float(h) + __high2float(h);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rsum;
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full[m]);
+    }
+    bool have_o = ok && T > 0;
+    if (have_o) {
+      have_o = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[m], (T - 1) & 1, abort, kWaitTimeoutNs, 9));
+      ptx::tc_fence_after();
+    }
+    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    if (p.splits == 1) {
+      __nv_bfloat16* orow = p.out + b * p.o_sb + static_cast<int64_t>(q) * p.o_ss + static_cast<int64_t>(head) * p.o_sh;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        float o[32];
+        if (have_o) {
+          ptx::tmem_ld32(t_o + ch * 32, o);
+          ptx::tmem_wait_ld();
+        }
+        if (valid_row) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = (have_o && l > 0.f) ? o[2 * i] * inv_l : 0.f;
+            const float a1 = (have_o && l > 0.f) ? o[2 * i + 1] * inv_l : 0.f;
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    } else {
+      const int64_t rows = static_cast<int64_t>(p.B) * p.Sq * p.Hq;
+      const int64_t wrow = static_cast<int64_t>(split) * rows + (static_cast<int64_t>(b) * p.Sq + q) * p.Hq + head;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        float o[32];
+        if (have_o) {
+          ptx::tmem_ld32(t_o + ch * 32, o);
+          ptx::tmem_wait_ld();
+        }
+        if (valid_row) {
+          float4* dst = reinterpret_cast<float4*>(p.ws_o + wrow * kHeadDim + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const bool live = have_o && l > 0.f;
+            dst[i] = make_float4(live ? o[4 * i] * inv_l : 0.f, live ? o[4 * i + 1] * inv_l : 0.f,
+                                 live ? o[4 * i + 2] * inv_l : 0.f, live ? o[4 * i + 3] * inv_l : 0.f);
+          }
+        }
+      }
+      if (valid_row) p.ws_lse[wrow] = (have_o && l > 0.f) ? m_used + __log2f(l) : -INFINITY;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Merge split-KV partials: one warp per output row, 4 head dims per lane.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ ws_o,
+                                                           const float* __restrict__ ws_lse,
+                                                           __nv_bfloat16* __restrict__ out, int splits, int B,
+                                                           int Sq, int Hq, int64_t o_sb, int64_t o_ss,
+                                                           int64_t o_sh) {
+  const int64_t rows = static_cast<int64_t>(B) * Sq * Hq;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, ws_lse[s * rows + row]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const float lse = ws_lse[s * rows + row];
+      if (lse == -INFINITY) continue;
+      const float w = ptx::ex2(lse - mx);
+      const float4 o = reinterpret_cast<const float4*>(ws_o + (s * rows + row) * kHeadDim)[lane];
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+      den += w;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const int64_t h = row % Hq;
+  const int64_t bq = row / Hq;
+  const int64_t q = bq % Sq;
+  const int64_t b = bq / Sq;
+  __nv_bfloat16* o = out + b * o_sb + q * o_ss + h * o_sh + lane * 4;
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  uint2 v;
+  v.x = *reinterpret_cast<const uint32_t*>(&lo);
+  v.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(o) = v;
+}
+
+}  // namespace fdl

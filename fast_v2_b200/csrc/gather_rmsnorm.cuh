@@ -1,0 +1,168 @@
+// (c) Fused gather + RMSNorm.  One warp per output row: the gathered row is
+// loaded once into registers with 16-byte loads (VPL vectors per lane), the
+// sum of squares is accumulated in fp32 (per-lane sequential FMA, then an
+// xor-butterfly), and both outputs (the gathered copy and the normalised row)
+// are written from registers -- one HBM read and one or two HBM writes per
+// element, nothing else.
+#pragma once
+#include "common.cuh"
+
+namespace fdl {
+
+constexpr int kNormThreads = 128;  // 4 rows per CTA
+
+struct NormArgs {
+  const char* x;
+  const int64_t* idx;
+  int64_t idx_sb;
+  const char* w;
+  char* gathered;
+  char* normed;
+  float eps;
+  int B, S, T, H;
+  int64_t x_sb, x_ss, o_sb, o_ss;  // bytes
+};
+
+template <typename T> struct ElemOps;
+template <> struct ElemOps<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct ElemOps<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct ElemOps<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+
+// Normalise one element.  16-bit inputs follow Fast_dLLM_QwenRMSNorm.forward:
+// round(x * inv) to the input dtype, then round(w * that).  fp32 inputs follow
+// select_gather_rmsnorm_kernel: x * inv * w in fp32.
+template <typename T>
+__device__ __forceinline__ T norm_elem(float x, float inv, const T* w, int i) {
+  if constexpr (sizeof(T) == 4) {
+    float n = __fmul_rn(x, inv);
+    if (w) n = __fmul_rn(n, ElemOps<T>::to_f(w[i]));
+    return ElemOps<T>::from_f(n);
+  } else {
+    T n = ElemOps<T>::from_f(__fmul_rn(x, inv));
+    if (w) n = ElemOps<T>::from_f(__fmul_rn(ElemOps<T>::to_f(w[i]), ElemOps<T>::to_f(n)));
+    return n;
+  }
+}
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __grid_constant__ NormArgs a) {
+  constexpr int EPV = 16 / sizeof(T);  // elements per 16-byte vector
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= a.B * a.T) return;
+  const int b = row / a.T;
+  const int t = row - b * a.T;
+  int64_t src_t = a.idx ? a.idx[b * a.idx_sb + t] : t;
+  if (src_t < 0 || src_t >= a.S) {
+    if (lane == 0) report(FDL_DEV_INDEX, src_t);
+    return;
+  }
+  const char* xr = a.x + b * a.x_sb + src_t * a.x_ss;
+  const int nvec = a.H / EPV;
+  uint4 v[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nvec) v[k] = ld_stream16(xr + vi * 16);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nvec) {
+      const T* e = reinterpret_cast<const T*>(&v[k]);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) {
+        const float f = ElemOps<T>::to_f(e[j]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(a.H)), a.eps));
+
+  char* gr = a.gathered ? a.gathered + b * a.o_sb + t * a.o_ss : nullptr;
+  char* nr = a.normed + b * a.o_sb + t * a.o_ss;
+  const T* w = reinterpret_cast<const T*>(a.w);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nvec) {
+      if (gr) st_stream16(gr + vi * 16, v[k]);
+      const T* e = reinterpret_cast<const T*>(&v[k]);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) oe[j] = norm_elem<T>(ElemOps<T>::to_f(e[j]), inv, w, vi * EPV + j);
+      st_stream16(nr + vi * 16, o);
+    }
+  }
+}
+
+// Generic path (any H, any alignment): one warp per row, two passes over the
+// row, scalar loads.  Same accumulation order per lane (element i goes to lane
+// (i / EPV) % 32, sequential within a lane) so results match the vector path.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_generic_kernel(const __grid_constant__ NormArgs a) {
+  constexpr int EPV = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= a.B * a.T) return;
+  const int b = row / a.T;
+  const int t = row - b * a.T;
+  int64_t src_t = a.idx ? a.idx[b * a.idx_sb + t] : t;
+  if (src_t < 0 || src_t >= a.S) {
+    if (lane == 0) report(FDL_DEV_INDEX, src_t);
+    return;
+  }
+  const T* xr = reinterpret_cast<const T*>(a.x + b * a.x_sb + src_t * a.x_ss);
+  float acc = 0.f;
+  for (int base = lane * EPV; base < a.H; base += 32 * EPV) {
+    for (int j = 0; j < EPV && base + j < a.H; ++j) {
+      const float f = ElemOps<T>::to_f(xr[base + j]);
+      acc = __fmaf_rn(f, f, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(a.H)), a.eps));
+  T* gr = a.gathered ? reinterpret_cast<T*>(a.gathered + b * a.o_sb + t * a.o_ss) : nullptr;
+  T* nr = reinterpret_cast<T*>(a.normed + b * a.o_sb + t * a.o_ss);
+  const T* w = reinterpret_cast<const T*>(a.w);
+  for (int i = lane; i < a.H; i += 32) {
+    const T xv = xr[i];
+    if (gr) gr[i] = xv;
+    nr[i] = norm_elem<T>(ElemOps<T>::to_f(xv), inv, w, i);
+  }
+}
+
+template <typename T>
+inline void launch_gather_rmsnorm(const NormArgs& a, bool vec_ok, cudaStream_t s) {
+  const int rows = a.B * a.T;
+  const dim3 grid((rows + 3) / 4);
+  const int nvec = a.H * static_cast<int>(sizeof(T)) / 16;
+  if (!vec_ok || nvec > 32 * 32) {
+    gather_rmsnorm_generic_kernel<T><<<grid, kNormThreads, 0, s>>>(a);
+    return;
+  }
+  const int vpl = (nvec + 31) / 32;
+  if (vpl <= 2) gather_rmsnorm_kernel<T, 2><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 4) gather_rmsnorm_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 8) gather_rmsnorm_kernel<T, 8><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 14) gather_rmsnorm_kernel<T, 14><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 16) gather_rmsnorm_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 28) gather_rmsnorm_kernel<T, 28><<<grid, kNormThreads, 0, s>>>(a);
+  else gather_rmsnorm_kernel<T, 32><<<grid, kNormThreads, 0, s>>>(a);
+}
+
+}  // namespace fdl

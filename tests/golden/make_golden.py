@@ -1,0 +1,227 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE's own
+Python code (navneet-13/fast_v2) on CPU.
+
+Usage:  python tests/golden/make_golden.py [/path/to/reference]
+
+The reference is imported read-only.  Its modeling.py needs three small shims
+on transformers 5.x (a stub ``configuration`` module with ``bd_size``, and
+nothing else for the functions used here); they are defined below and touch
+nothing but this process.  Each fixture stores the seeded inputs and the
+reference outputs; tests/test_oracle_golden.py pins the CPU oracle to them and
+the GPU parity tests compare the CUDA path with them.  Only this script reads
+the reference; the fixtures travel, the reference does not.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FV2_REFERENCE", "/root/reference"))
+MODELING = REF / "models/models--Efficient-Large-Model--Fast_dLLM_v2_7B/snapshots/0661abf5f9f0ee338970d091052a26c8efa51974/modeling.py"
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def load_reference():
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(REF / "cuda_bench"))
+    pkg = types.ModuleType("fdllm_ref_pkg")
+    pkg.__path__ = [str(MODELING.parent)]
+    sys.modules["fdllm_ref_pkg"] = pkg
+    from transformers import Qwen2Config
+
+    cfg = types.ModuleType("fdllm_ref_pkg.configuration")
+
+    class Fast_dLLM_QwenConfig(Qwen2Config):  # modeling.py:28 imports this name
+        model_type = "fast_dllm_qwen_stub"
+
+        def __init__(self, bd_size=32, **kw):
+            self.bd_size = bd_size
+            super().__init__(**kw)
+
+    cfg.Fast_dLLM_QwenConfig = Fast_dLLM_QwenConfig
+    sys.modules["fdllm_ref_pkg.configuration"] = cfg
+    spec = importlib.util.spec_from_file_location("fdllm_ref_pkg.modeling", MODELING)
+    modeling = importlib.util.module_from_spec(spec)
+    sys.modules["fdllm_ref_pkg.modeling"] = modeling
+    spec.loader.exec_module(modeling)
+    import utils.attention_backends as ab
+    import utils.block_sparse_cache as bsc
+    import utils.dynamic_block_kv as dbk
+    import utils.static_kv_cache as skv
+    import test_correctness as tc
+
+    return types.SimpleNamespace(modeling=modeling, skv=skv, dbk=dbk, bsc=bsc, ab=ab, tc=tc)
+
+
+def gen_static_kv(ref):
+    """StaticKVCache: prefill update (ragged 40), commit update (32), scratch write
+    at kv_write_start, write_sparse with a repeated position."""
+    g = torch.Generator().manual_seed(0)
+    B, S, L, H, D = 2, 96, 2, 2, 64
+    c = ref.skv.StaticKVCache(B, S, L, H, D, torch.bfloat16, torch.device("cpu"))
+    out = {}
+    rnd = lambda *shape: torch.randn(*shape, generator=g).to(torch.bfloat16)  # noqa: E731
+    for step, s_len in (("pre", 40), ("commit", 32)):
+        for l in range(L):
+            k, v = rnd(B, s_len, H, D), rnd(B, s_len, H, D)
+            out[f"{step}_k{l}"], out[f"{step}_v{l}"] = bits(k), bits(v)
+            c.update(k, v, l)
+    out["seq_len_after_commit"] = np.int64(c.get_seq_length())
+    out["cache_seqlens"] = c.cache_seqlens.numpy().copy()
+    c.set_kv_write_start(c.get_seq_length())
+    c.set_scratch_seqlens(c.get_seq_length() + 16)
+    c.prepare_write_idx(16)
+    for l in range(L):
+        k, v = rnd(B, 16, H, D), rnd(B, 16, H, D)
+        out[f"scratch_k{l}"], out[f"scratch_v{l}"] = bits(k), bits(v)
+        c.write_scratch_compiled(k, v, l)
+    pos = torch.tensor([[3, 50, 51, 90, 7], [10, 11, 10, 95, 0]], dtype=torch.int64)
+    out["sparse_pos"] = pos.numpy()
+    for l in range(L):
+        k, v = rnd(B, 5, H, D), rnd(B, 5, H, D)
+        out[f"sparse_k{l}"], out[f"sparse_v{l}"] = bits(k), bits(v)
+        c.write_sparse(k, v, l, pos)
+    for l in range(L):
+        out[f"final_k{l}"], out[f"final_v{l}"] = bits(c.key_cache[l]), bits(c.value_cache[l])
+    out["scratch_seqlens"] = c.scratch_seqlens.numpy().copy()
+    np.savez_compressed(HERE / "static_kv.npz", **out)
+
+
+def gen_dynamic_block(ref):
+    """DynamicBlockKV write_full + scatter with _dkv_fed_indices padding
+    (repeated first index), and BlockSparseCache scatter of hidden rows."""
+    g = torch.Generator().manual_seed(1)
+    B, H, blk, D, L = 2, 2, 32, 64, 2
+    buf = ref.dbk.DynamicBlockKV(0, L, B, H, blk, D, torch.bfloat16, torch.device("cpu"))
+    prv = torch.zeros(B, blk, dtype=torch.bool)
+    prv[0, 2:30] = True
+    prv[1, ::3] = True
+    fed, n_fed = ref.modeling.Fast_dLLM_QwenForCausalLM._dkv_fed_indices(prv)
+    out = {"prv": prv.numpy(), "fed": fed.numpy(), "n_fed": np.int64(n_fed)}
+    for l in range(L):
+        kf = torch.randn(B, H, blk, D, generator=g).to(torch.bfloat16)
+        vf = torch.randn(B, H, blk, D, generator=g).to(torch.bfloat16)
+        buf.write_full(l, kf, vf)
+        ks = torch.randn(B, H, n_fed, D, generator=g).to(torch.bfloat16)
+        vs = torch.randn(B, H, n_fed, D, generator=g).to(torch.bfloat16)
+        buf.write(l, ks, vs, fed)
+        gk, gv = buf.get(l)
+        out.update({f"full_k{l}": bits(kf), f"full_v{l}": bits(vf), f"sel_k{l}": bits(ks), f"sel_v{l}": bits(vs),
+                    f"final_k{l}": bits(gk), f"final_v{l}": bits(gv)})
+    hid = 256
+    bs = ref.bsc.BlockSparseCache(L, B, blk, hid, torch.bfloat16, torch.device("cpu"))
+    base = torch.randn(B, blk, hid, generator=g).to(torch.bfloat16)
+    bs.cache_attn_output(1, base)
+    tok = torch.tensor([[0, 5, 31], [4, 4, 9]], dtype=torch.int64)
+    vals = torch.randn(B, 3, hid, generator=g).to(torch.bfloat16)
+    bs.scatter_attn_output(1, tok, vals)
+    out.update({"bsc_base": bits(base), "bsc_tok": tok.numpy(), "bsc_vals": bits(vals),
+                "bsc_final": bits(bs.get_attn_output(1))})
+    np.savez_compressed(HERE / "dynamic_block.npz", **out)
+
+
+def gen_rmsnorm(ref):
+    """ref_gather_input_rmsnorm (cuda_bench/test_correctness.py:33-50) on the
+    reference's own case grid (test_correctness.py:128-144), with a
+    non-trivial weight; the H=3584 case is shortened to S=64 rows."""
+    cases_bf16 = [(1, 64, 128, 7, 1e-6), (2, 128, 256, 16, 1e-5), (1, 64, 3584, 32, 1e-6), (2, 256, 512, 24, 1e-6)]
+    cases_f32 = [(1, 32, 64, 5, 1e-6), (3, 48, 96, 11, 1e-6), (1, 128, 512, 40, 1e-6)]
+    out = {}
+    for tag, dt, cases in (("bf16", torch.bfloat16, cases_bf16), ("f32", torch.float32, cases_f32)):
+        for i, (b, s, h, t, eps) in enumerate(cases):
+            g = torch.Generator().manual_seed(100 + i)
+            x = torch.randn(b, s, h, generator=g).to(dt)
+            idx = torch.randint(0, s, (b, t), generator=g, dtype=torch.long)
+            w = (1.0 + 0.1 * torch.randn(h, generator=g)).to(dt)
+            gath, normed = ref.tc.ref_gather_input_rmsnorm(x, idx, w, eps)
+            key = f"{tag}_{i}"
+            conv = bits if dt == torch.bfloat16 else (lambda z: z.numpy())
+            out.update({f"{key}_x": conv(x), f"{key}_idx": idx.numpy(), f"{key}_w": conv(w),
+                        f"{key}_eps": np.float64(eps), f"{key}_gathered": conv(gath), f"{key}_normed": conv(normed)})
+        out[f"{tag}_n"] = np.int64(len(cases))
+    np.savez_compressed(HERE / "rmsnorm.npz", **out)
+
+
+def gen_attention(ref):
+    """flash_kvcache_attention semantics through the reference's SDPA backend
+    (AttentionBackend._sdpa_attention, utils/attention_backends.py:362-383) with
+    the per-batch seqused mask of StaticKVCache.get_seqused_mask_batched
+    (utils/static_kv_cache.py:295-302), in fp32 on bf16-representable inputs;
+    plus the dynamic path: repeat_kv + SDPA over cat(prefix, block) under
+    eval_mask (modeling.py:202-211, 390-411, 585-593) with a prefix of 40."""
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    B, Sq, Hq, Hkv, D, S = 2, 32, 14, 2, 128, 160
+    q = (torch.randn(B, Sq, Hq, D, generator=g) / D ** 0.5).to(torch.bfloat16)
+    k = torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16)
+    seqlens = torch.tensor([130, 69], dtype=torch.int32)
+    cache = ref.skv.StaticKVCache(B, S, 1, Hkv, D, torch.float32, torch.device("cpu"))
+    mask = cache.get_seqused_mask_batched(seqlens)
+    be = ref.ab.AttentionBackend(ref.ab.AttentionBackend.SDPA, None)
+    o = be._sdpa_attention(q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2), mask,
+                           D ** -0.5, False, 0.0).transpose(1, 2)
+    out.update({"kv_q": bits(q), "kv_k": bits(k), "kv_v": bits(v), "kv_seqlens": seqlens.numpy(),
+                "kv_out": o.contiguous().numpy()})
+    # dynamic path: BHSD prefix of 40 + block of 32, block-causal eval_mask
+    P, blk = 40, 32
+    qd = (torch.randn(1, Hq, blk, D, generator=g) / D ** 0.5).to(torch.bfloat16)
+    pk = torch.randn(1, Hkv, P, D, generator=g).to(torch.bfloat16)
+    pv = torch.randn(1, Hkv, P, D, generator=g).to(torch.bfloat16)
+    bk = torch.randn(1, Hkv, blk, D, generator=g).to(torch.bfloat16)
+    bv = torch.randn(1, Hkv, blk, D, generator=g).to(torch.bfloat16)
+    fk = torch.cat((pk, bk), dim=-2).float()
+    fv = torch.cat((pv, bv), dim=-2).float()
+    m = ref.modeling.Fast_dLLM_QwenModel.eval_mask(None, blk, blk, P)
+    n_rep = Hq // Hkv
+    od = torch.nn.functional.scaled_dot_product_attention(
+        qd.float(), ref.modeling.repeat_kv(fk, n_rep), ref.modeling.repeat_kv(fv, n_rep), attn_mask=m,
+        scale=D ** -0.5).transpose(1, 2)
+    out.update({"dyn_q": bits(qd), "dyn_pk": bits(pk), "dyn_pv": bits(pv), "dyn_bk": bits(bk), "dyn_bv": bits(bv),
+                "dyn_mask": m.numpy(), "dyn_out": od.contiguous().numpy(),
+                "dyn_repeat_k": bits(ref.modeling.repeat_kv(torch.cat((pk, bk), dim=-2), n_rep))})
+    np.savez_compressed(HERE / "attention.npz", **out)
+
+
+def gen_index_ops(ref):
+    """_dkv_fed_indices, _focus_update_frozen and eval_mask known answers."""
+    g = torch.Generator().manual_seed(11)
+    M = ref.modeling.Fast_dLLM_QwenForCausalLM
+    out = {}
+    for i in range(6):
+        prv = torch.rand(4, 32, generator=g) < (0.15 * i)
+        fed, n = M._dkv_fed_indices(prv)
+        out[f"fed_prv_{i}"], out[f"fed_idx_{i}"], out[f"fed_n_{i}"] = prv.numpy(), fed.numpy(), np.int64(n)
+        mask = torch.rand(4, 32, generator=g) < 0.5
+        frozen = torch.rand(4, 32, generator=g) < 0.2
+        out[f"frz_mask_{i}"], out[f"frz_in_{i}"] = mask.numpy(), frozen.numpy()
+        out[f"frz_out_{i}"] = M._focus_update_frozen(frozen, mask).numpy()
+    for cl in (0, 40, 64):
+        out[f"eval_mask_{cl}"] = ref.modeling.Fast_dLLM_QwenModel.eval_mask(None, 32, 32, cl).numpy()
+    np.savez_compressed(HERE / "index_ops.npz", **out)
+
+
+def main():
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    ref = load_reference()
+    gen_static_kv(ref)
+    gen_dynamic_block(ref)
+    gen_rmsnorm(ref)
+    gen_attention(ref)
+    gen_index_ops(ref)
+    for p in sorted(HERE.glob("*.npz")):
+        print(f"{p.name}: {p.stat().st_size / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()

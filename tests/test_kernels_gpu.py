@@ -1,0 +1,294 @@
+"""GPU parity of every kernel of the C ABI against the CPU oracle and the
+reference's golden vectors.  Bit-exact for copies and index selection;
+max-abs 2e-2 / rel 1e-2 for RMSNorm and attention (bf16)."""
+import numpy as np
+import pytest
+import torch
+
+from fast_v2_b200 import _lib
+from oracle import kvcache_oracle as O
+from tests._util import assert_close, bits_of, golden, t_from_bits
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2  # bf16 tolerance of the north-star bound
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _ops():
+    _lib.ensure_ops()
+    _lib.last_device_error()
+    yield
+    code, info = _lib.last_device_error()
+    assert code == 0, f"device error {code} (info {info}) left by the test"
+
+
+def rbf16(shape, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------ (a)
+def test_kv_append_per_sequence_starts_bit_exact():
+    L, B, S, H, D, n = 3, 5, 300, 4, 128, 32
+    kc = [rbf16((B, S, H, D), 10 + l) for l in range(L)]
+    vc = [rbf16((B, S, H, D), 20 + l) for l in range(L)]
+    ks = [rbf16((B, n, H, D), 30 + l) for l in range(L)]
+    vs = [rbf16((B, n, H, D), 40 + l) for l in range(L)]
+    start = torch.tensor([0, 17, 268, 100, 31], dtype=torch.int32)
+    gk = [t.to(DEV) for t in kc]
+    gv = [t.to(DEV) for t in vc]
+    torch.ops.fdl.kv_append(gk, gv, [t.to(DEV) for t in ks], [t.to(DEV) for t in vs], start.to(DEV))
+    for l in range(L):
+        ek, ev = bits_of(kc[l]).copy(), bits_of(vc[l]).copy()
+        O.kv_append(ek, ev, bits_of(ks[l]), bits_of(vs[l]), start.numpy())
+        assert np.array_equal(bits_of(gk[l]), ek) and np.array_equal(bits_of(gv[l]), ev)
+
+
+def test_kv_append_out_of_range_reports_not_faults():
+    B, S, H, D = 2, 40, 4, 128
+    k = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device=DEV)
+    v = torch.zeros_like(k)
+    src = torch.ones(B, 32, H, D, dtype=torch.bfloat16, device=DEV)
+    start = torch.tensor([0, 20], dtype=torch.int32, device=DEV)  # row 1 overflows at 40
+    torch.ops.fdl.kv_append([k], [v], [src], [src], start)
+    code, info = _lib.last_device_error()
+    assert code == 1 and info >= S
+    assert float(k[1, 20:40].float().min()) == 1.0  # in-range part written
+    assert float(k[0, 32:].float().abs().max()) == 0.0
+
+
+def test_static_kv_golden_sequence_on_gpu():
+    g = golden("static_kv")
+    B, S, H, D = g["final_k0"].shape
+    for l in range(2):
+        kc = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device=DEV)
+        vc = torch.zeros_like(kc)
+        for name, start in (("pre", 0), ("commit", 40), ("scratch", 72)):
+            st = torch.full((B,), start, dtype=torch.int32, device=DEV)
+            torch.ops.fdl.kv_append([kc], [vc], [t_from_bits(g[f"{name}_k{l}"], DEV)],
+                                    [t_from_bits(g[f"{name}_v{l}"], DEV)], st)
+        torch.ops.fdl.kv_scatter(kc, vc, t_from_bits(g[f"sparse_k{l}"], DEV), t_from_bits(g[f"sparse_v{l}"], DEV),
+                                 torch.from_numpy(g["sparse_pos"]).to(DEV), 1)
+        assert np.array_equal(bits_of(kc), g[f"final_k{l}"]) and np.array_equal(bits_of(vc), g[f"final_v{l}"])
+
+
+def test_scatter_bhsd_and_hidden_rows_golden():
+    g = golden("dynamic_block")
+    fed = torch.from_numpy(g["fed"]).to(DEV)
+    for l in range(2):
+        k = t_from_bits(g[f"full_k{l}"], DEV).clone()
+        v = t_from_bits(g[f"full_v{l}"], DEV).clone()
+        torch.ops.fdl.kv_scatter(k, v, t_from_bits(g[f"sel_k{l}"], DEV), t_from_bits(g[f"sel_v{l}"], DEV), fed, 2)
+        assert np.array_equal(bits_of(k), g[f"final_k{l}"]) and np.array_equal(bits_of(v), g[f"final_v{l}"])
+    base = t_from_bits(g["bsc_base"], DEV).clone()
+    torch.ops.fdl.kv_scatter(base, None, t_from_bits(g["bsc_vals"], DEV), None,
+                             torch.from_numpy(g["bsc_tok"]).to(DEV), 1)
+    assert np.array_equal(bits_of(base), g["bsc_final"])
+
+
+@pytest.mark.parametrize("n", [1, 7, 32, 200])
+def test_scatter_duplicates_last_wins(n):
+    B, S, H, D = 3, 256, 4, 128
+    rng = np.random.default_rng(n)
+    pos = rng.integers(0, 40, size=(B, n)).astype(np.int64)  # many repeats
+    dst = rbf16((B, S, H, D), 1)
+    src = rbf16((B, n, H, D), 2)
+    exp = bits_of(dst).copy()
+    O.scatter_rows(exp, bits_of(src), pos)
+    gd = dst.to(DEV)
+    torch.ops.fdl.kv_scatter(gd, None, src.to(DEV), None, torch.from_numpy(pos).to(DEV), 1)
+    assert np.array_equal(bits_of(gd), exp)
+
+
+# ------------------------------------------------------------------ (b)
+def test_gather_prefix_packed_gqa_expand_with_block():
+    B, S, H, D, rep, nb = 4, 512, 4, 128, 7, 32
+    kc, vc = rbf16((B, S, H, D), 3), rbf16((B, S, H, D), 4)
+    kb, vb = rbf16((B, nb, H, D), 5), rbf16((B, nb, H, D), 6)
+    lens = np.array([256, 0, 511, 300], np.int32)
+    ek, cu = O.gather_prefix_packed(bits_of(kc), lens, rep, bits_of(kb))
+    ev, _ = O.gather_prefix_packed(bits_of(vc), lens, rep, bits_of(vb))
+    ok = torch.empty(int(cu[-1]), H * rep, D, dtype=torch.bfloat16, device=DEV)
+    ov = torch.empty_like(ok)
+    torch.ops.fdl.kv_gather_prefix(kc.to(DEV), vc.to(DEV), torch.from_numpy(lens).to(DEV), kb.to(DEV), vb.to(DEV),
+                                   rep, ok, ov, torch.from_numpy(cu).to(DEV), 1, 1)
+    assert np.array_equal(bits_of(ok), ek) and np.array_equal(bits_of(ov), ev)
+
+
+def test_gather_prefix_dynamic_concat_bhsd_golden():
+    g = golden("attention")
+    pk, pv = t_from_bits(g["dyn_pk"], DEV), t_from_bits(g["dyn_pv"], DEV)
+    bk, bv = t_from_bits(g["dyn_bk"], DEV), t_from_bits(g["dyn_bv"], DEV)
+    B, H, P, D = pk.shape
+    ok = torch.empty(B, H * 7, P + 32, D, dtype=torch.bfloat16, device=DEV)
+    ov = torch.empty_like(ok)
+    lens = torch.full((B,), P, dtype=torch.int32, device=DEV)
+    torch.ops.fdl.kv_gather_prefix(pk, pv, lens, bk, bv, 7, ok, ov, None, 2, 2)
+    assert np.array_equal(bits_of(ok), g["dyn_repeat_k"])
+
+
+def test_gather_rows_int32_and_int64_with_count():
+    B, S, H, D, n = 3, 100, 4, 128, 20
+    src = rbf16((B, S, H, D), 8)
+    rng = np.random.default_rng(1)
+    idx = np.stack([np.sort(rng.choice(S, n, replace=False)) for _ in range(B)]).astype(np.int64)
+    exp = O.gather_rows(bits_of(src), idx)
+    for dt in (torch.int64, torch.int32):
+        out = torch.zeros(B, n, H, D, dtype=torch.bfloat16, device=DEV)
+        cnt = torch.tensor([n, 5, 0], dtype=torch.int32, device=DEV)
+        torch.ops.fdl.kv_gather_rows(src.to(DEV), None, torch.from_numpy(idx).to(dt).to(DEV), cnt, out, None, 1)
+        o = bits_of(out)
+        assert np.array_equal(o[0], exp[0])
+        assert np.array_equal(o[1, :5], exp[1, :5]) and not o[1, 5:].any()
+        assert not o[2].any()
+
+
+@pytest.mark.parametrize("cap,lens", [(300, [300, 1, 77]), (2048, [2048, 1500, 0, 256]), (4096, [4096])])
+def test_sparse_prefix_select_and_gather_bit_exact(cap, lens):
+    B, H, D = len(lens), 4, 128
+    rng = np.random.default_rng(cap)
+    kb = O.f32_to_bf16(rng.standard_normal((B, cap, H, D)).astype(np.float32))
+    vb = O.f32_to_bf16(rng.standard_normal((B, cap, H, D)).astype(np.float32))
+    kb[0, 5] = kb[0, 9] = kb[0, 0]  # ties
+    lens = np.array(lens, np.int32)
+    sel_ref, keep_ref = O.sparse_prefix_select(kb, lens)
+    mk = sel_ref.shape[1]
+    k, v = t_from_bits(kb, DEV), t_from_bits(vb, DEV)
+    sel = torch.empty(B, mk, dtype=torch.int32, device=DEV)
+    out_len = torch.empty(B, dtype=torch.int32, device=DEV)
+    ko = torch.zeros(B, mk, H, D, dtype=torch.bfloat16, device=DEV)
+    vo = torch.zeros_like(ko)
+    ws = torch.empty(_lib.sparse_prefix_workspace_bytes(B, cap), dtype=torch.uint8, device=DEV)
+    torch.ops.fdl.kv_sparse_prefix(k, v, torch.from_numpy(lens).to(DEV), 1, 4, sel, out_len, ko, vo, ws)
+    assert np.array_equal(out_len.cpu().numpy(), keep_ref)
+    assert np.array_equal(sel.cpu().numpy(), sel_ref)
+    for b in range(B):
+        kk = int(keep_ref[b])
+        assert np.array_equal(bits_of(ko)[b, :kk], kb[b, sel_ref[b, :kk]])
+        assert np.array_equal(bits_of(vo)[b, :kk], vb[b, sel_ref[b, :kk]])
+    score = O.key_norm_scores(kb, lens)
+    got_score = ws[: B * cap * 4].view(torch.float32).view(B, cap).cpu().numpy()
+    for b in range(B):
+        L = int(lens[b])
+        assert np.array_equal(got_score[b, :L].view(np.uint32), score[b, :L].view(np.uint32))
+
+
+# ------------------------------------------------------------------ (c)
+@pytest.mark.parametrize("tag", ["bf16", "f32"])
+def test_gather_rmsnorm_golden(tag):
+    g = golden("rmsnorm")
+    for i in range(int(g[f"{tag}_n"])):
+        k = f"{tag}_{i}"
+        if tag == "bf16":
+            x, w = t_from_bits(g[f"{k}_x"], DEV), t_from_bits(g[f"{k}_w"], DEV)
+        else:
+            x, w = torch.from_numpy(g[f"{k}_x"]).to(DEV), torch.from_numpy(g[f"{k}_w"]).to(DEV)
+        idx = torch.from_numpy(g[f"{k}_idx"]).to(DEV)
+        B, T = idx.shape
+        gath = torch.empty(B, T, x.shape[2], dtype=x.dtype, device=DEV)
+        normed = torch.empty_like(gath)
+        torch.ops.fdl.gather_rmsnorm(x, idx, w, float(g[f"{k}_eps"]), gath, normed)
+        if tag == "bf16":
+            assert np.array_equal(bits_of(gath), g[f"{k}_gathered"])
+            assert_close(k, normed.float().cpu().numpy(), O.bf16_to_f32(g[f"{k}_normed"]), ATOL, RTOL)
+            assert np.mean(bits_of(normed) != g[f"{k}_normed"]) < 0.01
+        else:
+            assert np.array_equal(gath.cpu().numpy(), g[f"{k}_gathered"])
+            assert_close(k, normed.cpu().numpy(), g[f"{k}_normed"], 1e-5, 1e-5)
+
+
+def test_gather_rmsnorm_config1_shape():
+    B, S, H, T = 4, 2048, 3584, 512
+    x = rbf16((B, S, H), 21)
+    idx = torch.stack([torch.sort(torch.randperm(S, generator=torch.Generator().manual_seed(b))[:T]).values
+                       for b in range(B)])
+    w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(5))).to(torch.bfloat16)
+    gath = torch.empty(B, T, H, dtype=torch.bfloat16, device=DEV)
+    normed = torch.empty_like(gath)
+    torch.ops.fdl.gather_rmsnorm(x.to(DEV), idx.to(DEV), w.to(DEV), 1e-6, gath, normed)
+    eg, en = O.gather_rmsnorm_bf16(bits_of(x), idx.numpy(), bits_of(w), 1e-6)
+    assert np.array_equal(bits_of(gath), eg)
+    assert_close("config1", normed.float().cpu().numpy(), O.bf16_to_f32(en), ATOL, RTOL)
+    assert np.mean(bits_of(normed) != en) < 0.01
+
+
+# ------------------------------------------------------------------ (d)
+def _run_attn(q, k, v, seqlens, splits=0, kb=None, vb=None, mask_block=0, q_pos=None):
+    out = torch.empty_like(q)
+    B, Sq, Hq, _ = q.shape
+    ns = splits if splits > 0 else _lib.attn_auto_splits(B, Sq, Hq, k.shape[2], k.shape[1],
+                                                          kb.shape[1] if kb is not None else 0)
+    wsb = _lib.attn_workspace_bytes(B, Sq, Hq, ns)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=DEV) if wsb > 0 else None
+    torch.ops.fdl.block_attn(q, k, v, seqlens, kb, vb, q_pos, mask_block, q.shape[-1] ** -0.5, out, ws, splits)
+    return out
+
+
+def test_block_attn_golden_static():
+    g = golden("attention")
+    q, k, v = (t_from_bits(g[n], DEV) for n in ("kv_q", "kv_k", "kv_v"))
+    seq = torch.from_numpy(g["kv_seqlens"]).to(DEV)
+    for splits in (1, 2, 0):
+        out = _run_attn(q, k, v, seq, splits)
+        assert_close(f"static splits={splits}", out.float().cpu().numpy(), g["kv_out"], ATOL, RTOL)
+
+
+def test_block_attn_golden_dynamic_block_source_and_mask():
+    g = golden("attention")
+    q = t_from_bits(g["dyn_q"], DEV).transpose(1, 2).contiguous()  # BSHD
+    pk = t_from_bits(g["dyn_pk"], DEV).transpose(1, 2).contiguous()
+    pv = t_from_bits(g["dyn_pv"], DEV).transpose(1, 2).contiguous()
+    bk = t_from_bits(g["dyn_bk"], DEV).transpose(1, 2).contiguous()
+    bv = t_from_bits(g["dyn_bv"], DEV).transpose(1, 2).contiguous()
+    P = pk.shape[1]
+    seq = torch.full((1,), P, dtype=torch.int32, device=DEV)
+    out = _run_attn(q, pk, pv, seq, 1, bk, bv, mask_block=32)
+    assert_close("dynamic", out.float().cpu().numpy(), g["dyn_out"], ATOL, RTOL)
+
+
+@pytest.mark.parametrize(
+    "B,Sq,Hq,Hkv,cap,lens,splits",
+    [
+        (2, 32, 28, 4, 600, [600, 77], 1),
+        (2, 32, 28, 4, 600, [600, 77], 3),
+        (3, 8, 28, 4, 1000, [1000, 0, 513], 0),   # sub-block rows, an empty sequence
+        (1, 40, 28, 4, 300, [300], 1),            # two query chunks (qc = 36)
+        (2, 32, 12, 2, 384, [384, 200], 0),       # 1.5B geometry (G = 6)
+        (1, 1, 8, 8, 130, [130], 1),              # G = 1, single query
+        (1, 32, 28, 4, 8224, [8224], 0),          # long prefix, auto split
+    ],
+)
+def test_block_attn_random_vs_oracle(B, Sq, Hq, Hkv, cap, lens, splits):
+    q = rbf16((B, Sq, Hq, 128), 31, 128 ** -0.5)
+    k = rbf16((B, cap, Hkv, 128), 32)
+    v = rbf16((B, cap, Hkv, 128), 33)
+    seqlens = torch.tensor(lens, dtype=torch.int32)
+    out = _run_attn(q.to(DEV), k.to(DEV), v.to(DEV), seqlens.to(DEV), splits)
+    ref = O.block_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), lens)
+    assert_close("attn", out.float().cpu().numpy(), ref, ATOL, RTOL)
+
+
+def test_block_attn_block_source_with_query_positions():
+    B, Sq, Hq, Hkv, cap, nb = 2, 8, 28, 4, 200, 32
+    q = rbf16((B, Sq, Hq, 128), 41, 128 ** -0.5)
+    k, v = rbf16((B, cap, Hkv, 128), 42), rbf16((B, cap, Hkv, 128), 43)
+    kb, vb = rbf16((B, nb, Hkv, 128), 44), rbf16((B, nb, Hkv, 128), 45)
+    lens = np.array([150, 64], np.int32)
+    qpos = np.stack([lens[b] + np.array([0, 3, 5, 9, 12, 20, 30, 31]) for b in range(B)]).astype(np.int32)
+    out = _run_attn(q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(lens).to(DEV), 0, kb.to(DEV), vb.to(DEV),
+                    32, torch.from_numpy(qpos).to(DEV))
+    ref = O.block_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), lens, k_blk=kb.float().numpy(),
+                            v_blk=vb.float().numpy(), mask_block=32, q_pos=qpos)
+    assert_close("attn+block", out.float().cpu().numpy(), ref, ATOL, RTOL)
+
+
+def test_flash_kvcache_functional_op():
+    B, Sq, Hq, Hkv, cap = 2, 32, 28, 4, 512
+    q = rbf16((B, Sq, Hq, 128), 51, 128 ** -0.5).to(DEV)
+    k, v = rbf16((B, cap, Hkv, 128), 52).to(DEV), rbf16((B, cap, Hkv, 128), 53).to(DEV)
+    seq = torch.tensor([512, 100], dtype=torch.int32, device=DEV)
+    out = torch.ops.fdl.flash_kvcache(q, k, v, seq, 128 ** -0.5, False)
+    ref = O.block_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), [512, 100])
+    assert_close("flash_kvcache", out.float().cpu().numpy(), ref, ATOL, RTOL)
