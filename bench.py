@@ -1,0 +1,564 @@
+#!/usr/bin/env python
+"""Benchmark of the Fast-dLLM v2 KV-cache hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config NAME]
+
+Prints ONE JSON line (rank 0).  Multi-GPU runs are launched by torchrun, one
+process per GPU; sequences are sharded across ranks (no data-path collective),
+so scaling is weak and `value` is the aggregate over ranks divided by the max
+over ranks of the device time.
+
+Configs (BASELINE.json `configs`):
+  gather_norm   fused gather + RMSNorm, x [4, 2048, 3584] bf16, 512 idx/row
+  kv_path       28-layer committed-block append + varlen prefix gather with
+                GQA-7 expansion, cache [16, 4096, 4, 128] per layer and K/V
+  block_attn    block attention Q [B, 32, 28, 128] over a prefix of P keys
+                (--attn-b, --attn-p, --attn-sq select the point)
+
+Inputs are seeded synthetic tensors (the reference's datasets and weights are
+not available offline).  Between timed steps the inputs rotate through buffer
+sets larger than the 126 MB L2 (or are larger than L2 themselves).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+# --------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+        self.window = None
+
+    def _run(self):
+        try:
+            p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                  "--format=csv,noheader,nounits", "-lms", "100"],
+                                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        try:
+            while not self._stop.is_set():
+                line = p.stdout.readline()
+                if not line:
+                    break
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    self.samples.append((time.time(), parts))
+        finally:
+            p.terminate()
+            try:
+                p.wait(timeout=5)
+            except Exception:
+                p.kill()
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        time.sleep(0.3)
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        time.sleep(0.25)
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t0, t1 = self.window if self.window else (0, 1e30)
+        inside = [s for _, s in ((t, s) for t, s in self.samples) if True]
+        win = [s for t, s in self.samples if t0 - 0.15 <= t <= t1 + 0.15] or inside[-3:]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(s[1]) for s in win if num(s[1]) is not None]
+        mx = [num(s[2]) for s in win if num(s[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in win for i in range(4) if s[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(win)}
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# --------------------------------------------------------------------------
+# kernel timing inside the timed region
+# --------------------------------------------------------------------------
+class KernelTimer:
+    """CUDA events around every launch of the dominant kernel (on the stream
+    it is launched on); `avg_ms` is its mean launch duration."""
+
+    def __init__(self):
+        self.pairs = []
+        self.active = False
+
+    def wrap(self, fn):
+        if not self.active:
+            return fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        r = fn()
+        e.record()
+        self.pairs.append((s, e))
+        return r
+
+    def avg_ms(self):
+        if not self.pairs:
+            return None
+        return sum(s.elapsed_time(e) for s, e in self.pairs) / len(self.pairs)
+
+
+# --------------------------------------------------------------------------
+# workloads (ours)
+# --------------------------------------------------------------------------
+def gen(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+def wl_gather_norm(args, rank, world, kt: KernelTimer):
+    import numpy as np
+
+    from fast_v2_b200 import ensure_ops
+
+    ensure_ops()
+    B, S, H, T = 4, 2048, 3584, 512
+    nbuf = max(2, math.ceil(3 * L2_BYTES / (B * S * H * 2)))
+    g = gen(1000 + rank)
+    xs = [torch.randn(B, S, H, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
+    idx = torch.stack([torch.sort(torch.randperm(S, generator=g)[:T]).values for _ in range(B)]).cuda()
+    w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda()
+    outs = [(torch.empty(B, T, H, dtype=torch.bfloat16, device="cuda"),
+             torch.empty(B, T, H, dtype=torch.bfloat16, device="cuda")) for _ in range(nbuf)]
+    alg_bytes = B * T * H * 2 * 3 + B * T * 8 + H * 2  # read rows, write gathered + normed, idx, w
+    state = {"i": 0}
+
+    def step():
+        i = state["i"] % nbuf
+        state["i"] += 1
+        torch.ops.fdl.gather_rmsnorm(xs[i], idx, w, 1e-6, outs[i][0], outs[i][1])
+
+    # end-to-end through the public API with host buffers
+    from fast_v2_b200.cuda_bench.fused_sparse_extension import fused_gather_input_rmsnorm_pair
+
+    class _Norm(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight = torch.nn.Parameter(w, requires_grad=False)
+            self.variance_epsilon = 1e-6
+
+    norm = _Norm()
+    hx = xs[0].cpu().pin_memory()
+    hidx = idx.cpu().pin_memory()
+    hg = torch.empty(B, T, H, dtype=torch.bfloat16).pin_memory()
+    hn = torch.empty_like(hg).pin_memory()
+
+    def e2e_step():
+        dx = hx.to("cuda", non_blocking=True)
+        di = hidx.to("cuda", non_blocking=True)
+        gth, nrm = fused_gather_input_rmsnorm_pair(dx, di, norm)
+        hg.copy_(gth, non_blocking=True)
+        hn.copy_(nrm, non_blocking=True)
+
+    e2e_bytes = (hx.numel() * 2 + hidx.numel() * 8, hg.numel() * 2 + hn.numel() * 2)
+
+    def cpu_sample():
+        from oracle import torch_port
+
+        hxf = xs[0][:1].cpu()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 8.0 or n < 2:
+            torch_port.gather_input_rmsnorm(hxf, hidx[:1], w.cpu(), 1e-6)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return alg_bytes / 4 / dt / 1e9, f"{n} calls of batch row 1 of 4 ([1, 2048, 3584], 512 rows)"
+
+    return dict(
+        metric="fused gather+RMSNorm throughput (algorithmic HBM GB/s)", unit="GB/s",
+        units_per_step=alg_bytes / 1e9, step=step, dominant=step, graph=True, e2e_step=e2e_step,
+        e2e_bytes=e2e_bytes,
+        roofline=dict(bound="hbm", per_launch=alg_bytes, kernel="gather_rmsnorm_kernel"), launches_per_step=1,
+        config={"workload": "gather_norm", "x": [B, S, H], "rows_per_batch": T, "dtype": "bf16",
+                "l2": f"inputs rotate over {nbuf} buffer sets ({nbuf * B * S * H * 2 / 2**20:.0f} MiB > L2)"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
+def wl_kv_path(args, rank, world, kt: KernelTimer):
+    from fast_v2_b200 import ensure_ops
+
+    ensure_ops()
+    L, B, S, Hkv, D, rep, n = 28, 16, 4096, 4, 128, 7, 32
+    g = gen(2000 + rank)
+    lens = torch.randint(256, 2049, (B,), generator=g, dtype=torch.int32)
+    kc = [torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    vc = [torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    kn = [torch.randn(B, n, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    vn = [torch.randn(B, n, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    dlens = lens.cuda()
+    lens_after = (lens + n).cuda()
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens + n, 0)
+    total = int(cu[-1])
+    dcu = cu.cuda()
+    ok = torch.empty(total, Hkv * rep, D, dtype=torch.bfloat16, device="cuda")
+    ov = torch.empty_like(ok)
+    append_bytes = 2 * L * B * n * Hkv * D * 2 * 2  # K and V, read + write
+    gather_bytes_layer = total * Hkv * D * 2 * 2 * (1 + rep)  # read once, write rep times, K and V
+    alg = append_bytes + L * gather_bytes_layer
+
+    def gather(l):
+        torch.ops.fdl.kv_gather_prefix(kc[l], vc[l], lens_after, None, None, rep, ok, ov, dcu, 1, 1)
+
+    def step():
+        torch.ops.fdl.kv_append(kc, vc, kn, vn, dlens)
+        for l in range(L):
+            gather(l)
+
+    dstate = {"l": 0}
+
+    def dominant():
+        gather(dstate["l"] % L)
+        dstate["l"] += 1
+
+    def cpu_sample():
+        from oracle import torch_port
+
+        layers = [0, 1]
+        hk = [kc[l].cpu() for l in layers]
+        hv = [vc[l].cpu() for l in layers]
+        t0 = time.perf_counter()
+        torch_port.append_and_gather(hk, hv, kn[0].cpu(), vn[0].cpu(), lens, rep, range(len(layers)))
+        dt = (time.perf_counter() - t0) / len(layers) * L
+        return alg / dt / 1e9, "2 of 28 layers (append + gather + GQA expand), scaled to 28"
+
+    return dict(
+        metric="KV append + prefix gather throughput (algorithmic HBM GB/s)", unit="GB/s",
+        units_per_step=alg / 1e9, step=step, dominant=dominant, graph=True, e2e_step=None, e2e_bytes=None,
+        roofline=dict(bound="hbm", per_launch=gather_bytes_layer, kernel="kv_gather_prefix_kernel"),
+        launches_per_step=1 + L,
+        config={"workload": "kv_path", "layers": L, "batch": B, "cache": [B, S, Hkv, D], "block": n,
+                "gqa_rep": rep, "sum_len": total, "l2": f"working set {2 * L * B * S * Hkv * D * 2 / 2**30:.1f} GiB > L2"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
+def wl_block_attn(args, rank, world, kt: KernelTimer):
+    from fast_v2_b200 import _lib, ensure_ops
+
+    ensure_ops()
+    B, P, Sq, Hq, Hkv, D = args.attn_b, args.attn_p, args.attn_sq, 28, 4, 128
+    cap = P + 32
+    g = gen(3000 + rank)
+    kv_bytes = B * cap * Hkv * D * 2 * 2
+    nbuf = max(1, math.ceil(3 * L2_BYTES / kv_bytes)) if kv_bytes < 3 * L2_BYTES else 1
+    ks = [torch.randn(B, cap, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
+    vs = [torch.randn(B, cap, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
+    q = (torch.randn(B, Sq, Hq, D, generator=g) / math.sqrt(D)).to(torch.bfloat16).cuda()
+    seq = torch.full((B,), cap, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    splits = _lib.attn_auto_splits(B, Sq, Hq, Hkv, cap, 0)
+    wsb = _lib.attn_workspace_bytes(B, Sq, Hq, splits)
+    ws = torch.empty(max(1, wsb), dtype=torch.uint8, device="cuda")
+    flops = 4 * B * Hq * Sq * cap * D
+    state = {"i": 0}
+
+    def step():
+        i = state["i"] % nbuf
+        state["i"] += 1
+        torch.ops.fdl.block_attn(q, ks[i], vs[i], seq, None, None, None, 0, D ** -0.5, out,
+                                 ws if wsb > 0 else None, splits)
+
+    def cpu_sample():
+        from oracle import torch_port
+
+        bb = 1
+        hq, hk, hv = q[:bb].cpu(), ks[0][:bb].cpu(), vs[0][:bb].cpu()
+        t0 = time.perf_counter()
+        nrep = 0
+        while time.perf_counter() - t0 < 8.0 or nrep < 1:
+            torch_port.flash_kvcache_sdpa(hq, hk, hv, seq[:bb].cpu(), D ** -0.5)
+            nrep += 1
+        dt = (time.perf_counter() - t0) / nrep
+        return flops / B * bb / dt / 1e12, f"{nrep} calls of 1 of {B} sequences (SDPA, GQA expand, seqused mask)"
+
+    return dict(
+        metric="block attention throughput (TFLOP/s)", unit="TFLOP/s", units_per_step=flops / 1e12, step=step,
+        dominant=step, graph=True, e2e_step=None, e2e_bytes=None,
+        roofline=dict(bound="tensor", per_launch=flops, kernel="block_attn_kernel", hbm_bytes=kv_bytes),
+        launches_per_step=1 + (1 if splits > 1 else 0),
+        config={"workload": "block_attn", "batch": B, "prefix": P, "q_rows": Sq, "heads": [Hq, Hkv], "splits": splits,
+                "l2": f"K/V {kv_bytes / 2**20:.0f} MiB x {nbuf} buffer sets"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
+WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn}
+DEFAULT_CONFIG = "kv_path"
+
+
+# --------------------------------------------------------------------------
+# reference arm: the reference's torch path on the host CPU
+# --------------------------------------------------------------------------
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+
+    class _Noop:
+        active = False
+
+        def wrap(self, fn):
+            return fn()
+
+    # Build the same workload on CPU-sized samples: reuse the cpu_sample hooks,
+    # which time the restated reference torch path on this host.
+    import types
+
+    fake_args = types.SimpleNamespace(**vars(args))
+    if not torch.cuda.is_available():
+        raise SystemExit(json.dumps({"impl": "reference", "unavailable": "needs the GPU box to stage inputs"}))
+    w = WORKLOADS[args.config](fake_args, 0, 1, _Noop())
+    vals = []
+    for _ in range(args.warmup):
+        w["cpu_sample"]()
+    t_all = time.perf_counter()
+    sample = ""
+    for _ in range(args.steps):
+        v, sample = w["cpu_sample"]()
+        vals.append(v)
+    wall = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": w["metric"], "value": value, "unit": w["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / max(1, args.steps) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"],
+        "data": "synthetic", "config": w["config"],
+        "cpu_baseline": {"value": value, "unit": w["unit"], "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": w["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# --------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default=DEFAULT_CONFIG)
+    ap.add_argument("--attn-b", type=int, default=64)
+    ap.add_argument("--attn-p", type=int, default=8192)
+    ap.add_argument("--attn-sq", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {"gather_norm": 2000, "kv_path": 100, "block_attn": 200}.get(args.config, 20)
+    args.warmup = max(3, args.warmup)
+    world, rank, local = setup_dist()
+
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = load_peaks()
+    kt = KernelTimer()
+    w = WORKLOADS[args.config](args, rank, world, kt)
+    for _ in range(args.warmup):
+        w["step"]()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    graph = None
+    if w.get("graph"):
+        # Kernel-level configs: the K steps are replayed from a CUDA graph so
+        # the device time is not diluted by host dispatch gaps.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                w["step"]()
+        graph.replay()
+        barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier(world)
+    kt.active = not w.get("graph")
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    start.record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(args.steps):
+            w["step"]()
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    kt.active = False
+    sampler.mark(t0, t1)
+    barrier(world)
+    sampler.stop()
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    value = w["units_per_step"] * args.steps * world / (ms_max / 1e3)
+    del graph
+
+    # dominant-kernel duration: its own launches back to back in a CUDA graph,
+    # timed with events on the launching stream.
+    rf = w["roofline"]
+    kms = None
+    if w.get("dominant") is not None:
+        n_dom = max(20, min(500, args.steps))
+        gd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd):
+            for _ in range(n_dom):
+                w["dominant"]()
+        gd.replay()
+        torch.cuda.synchronize()
+        s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s1.record(stream)
+        gd.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        kms = s1.elapsed_time(e1) / n_dom
+        del gd
+    else:
+        kms = kt.avg_ms()
+    roof = None
+    if kms:
+        if rf["bound"] == "hbm":
+            ach = rf["per_launch"] / (kms / 1e3) / 1e9
+            peak = peaks["hbm_gbs"]
+            roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"],
+                    "launch_us": round(kms * 1e3, 2), "peak_src": peaks["src"]}
+        else:
+            ach = rf["per_launch"] / (kms / 1e3) / 1e12
+            peak = peaks["bf16_tflops"]
+            roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"],
+                    "launch_us": round(kms * 1e3, 2), "peak_src": peaks["src"]}
+            if rf.get("hbm_bytes"):
+                roof["hbm_gbs_achieved"] = round(rf["hbm_bytes"] / (kms / 1e3) / 1e9, 1)
+        tr = ROOT / "profiles" / "traffic.json"
+        if tr.exists():
+            t = json.loads(tr.read_text()).get(args.config)
+            if t:
+                roof["traffic"] = t
+
+    # end-to-end through the public API with host buffers
+    e2e = None
+    if w.get("e2e_step"):
+        for _ in range(2):
+            w["e2e_step"]()
+        barrier(world)
+        n_e2e = max(3, min(args.steps, 50))
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(n_e2e):
+            w["e2e_step"]()
+        e2.record()
+        torch.cuda.synchronize()
+        ms2 = max_over_ranks(s2.elapsed_time(e2), world)
+        e2e = {"value": w["units_per_step"] * n_e2e * world / (ms2 / 1e3), "unit": w["unit"],
+               "h2d_bytes_per_step": w["e2e_bytes"][0], "d2h_bytes_per_step": w["e2e_bytes"][1]}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        v, sample = w["cpu_sample"]()
+        cpu = {"value": v, "unit": w["unit"], "cores": torch.get_num_threads(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": w["metric"], "value": value, "unit": w["unit"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+            "config": {**w["config"], "parallelism": f"dp{world} (sequence-sharded replicas)"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": sampler.summary(),
+            "gpu_launches": w["launches_per_step"] * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,388 @@
+"""Block-diffusion decoding at Qwen2.5 geometry on the fdl KV-cache kernels.
+
+This is the end-to-end driver of the hot path: a Qwen2-architecture
+block-diffusion LM (random-init weights; the real checkpoints are not
+available offline) whose every KV-cache touch -- commit append, dKV block
+buffer writes, token-sparse prefix selection and gather, RMSNorm, and the
+block attention over cat(prefix, block) with in-kernel GQA -- runs on the
+sm_100a kernels of libfdl_b200.so.  The dense projections and the MLP are
+cuBLAS GEMMs through torch.
+
+The decode loop follows the reference's dKV sampler ``batch_sample_dkv``
+(generation_functions.py:2132-2340) and its forwards
+(``forward_dkv``, modeling.py:1625-1692; commit ``forward`` with
+``update_past_key_values=True``):
+
+* prefill the prompt (multiple of the block size), bridge token from the
+  last logit;
+* per block: 32-token block (bridge token + masks); sub-blocks of 8 decoded
+  by diffusion steps -- full-block steps on refresh boundaries
+  (step_in_block <= 1 or step_in_block % refresh == 0), otherwise cached
+  steps that feed only the not-yet-frozen positions
+  (``_dkv_fed_indices``, modeling.py:2039-2060) and read the other block K/V
+  from the DynamicBlockKV buffer; each step unmasks the tokens of the current
+  sub-block whose probability exceeds the threshold, and at least the most
+  confident one (generation_functions.py:2290-2305);
+* block complete: commit forward over the 32 final tokens appends their K/V
+  to the committed cache; its last logit gives the next bridge token.
+
+``sparse_prefix`` (a keep fraction, e.g. 0.25) replaces the committed prefix
+seen by the diffusion steps with the top-scoring prefix tokens by key norm,
+re-selected once per block (no reference counterpart; see
+include/fdl_kvcache.h, fdl_kv_sparse_prefix).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class Geometry:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+    tie_embeddings: bool = False
+
+    @property
+    def gqa(self) -> int:
+        return self.heads // self.kv_heads
+
+
+QWEN25_7B = Geometry(28, 3584, 28, 4, 128, 18944, 152064)
+QWEN25_1_5B = Geometry(28, 1536, 12, 2, 128, 8960, 151936, tie_embeddings=True)
+
+MASK_ID = 151665
+STOP_ID = 151645
+PAD_ID = 151643
+
+
+def param_count(g: Geometry) -> int:
+    per = (g.heads + 2 * g.kv_heads) * g.head_dim * (g.hidden + 1) + g.hidden * g.heads * g.head_dim
+    per += 3 * g.hidden * g.ffn + 2 * g.hidden
+    emb = g.vocab * g.hidden
+    return g.layers * per + emb * (1 if g.tie_embeddings else 2) + g.hidden
+
+
+class BlockDiffusionLM:
+    """Random-init Qwen2 block-diffusion LM (weights N(0, init_std), biases 0,
+    norm weights 1, as Fast_dLLM_QwenPreTrainedModel._init_weights,
+    modeling.py:511-522).  q/k/v and gate/up projections are stored fused."""
+
+    def __init__(self, geo: Geometry, device="cuda", dtype=torch.bfloat16, seed: int = 0, init_std: float = 0.02,
+                 init_device: str | None = None):
+        _lib.ensure_ops()
+        self.geo, self.device, self.dtype = geo, torch.device(device), dtype
+        g = geo
+        # Generation on the target device is fast; init_device="cpu" gives
+        # bit-reproducible weights across machines (used by the parity tests).
+        gd = torch.device(init_device) if init_device else self.device
+        gen = torch.Generator(device=gd).manual_seed(seed)
+
+        def normal(*shape):
+            return (torch.randn(*shape, generator=gen, device=gd, dtype=torch.float32) * init_std).to(dtype).to(
+                self.device)
+
+        qkv_out = (g.heads + 2 * g.kv_heads) * g.head_dim
+        self.embed = normal(g.vocab, g.hidden)
+        self.layers = []
+        for _ in range(g.layers):
+            self.layers.append(dict(
+                ln1=torch.ones(g.hidden, dtype=dtype, device=self.device),
+                wqkv=normal(qkv_out, g.hidden),
+                bqkv=torch.zeros(qkv_out, dtype=dtype, device=self.device),
+                wo=normal(g.hidden, g.heads * g.head_dim),
+                ln2=torch.ones(g.hidden, dtype=dtype, device=self.device),
+                wgu=normal(2 * g.ffn, g.hidden),
+                wd=normal(g.hidden, g.ffn),
+            ))
+        self.norm = torch.ones(g.hidden, dtype=dtype, device=self.device)
+        self.lm_head = self.embed if g.tie_embeddings else normal(g.vocab, g.hidden)
+        inv = 1.0 / (g.rope_theta ** (torch.arange(0, g.head_dim, 2, dtype=torch.int64).float() / g.head_dim))
+        self.inv_freq = inv.to(self.device)
+
+    # ------------------------------------------------------------------ ops
+    def rmsnorm(self, x, w):
+        out = torch.empty_like(x)
+        torch.ops.fdl.gather_rmsnorm(x, None, w, self.geo.eps, None, out)
+        return out
+
+    def rope(self, pos):
+        """cos/sin [B, T, D] for integer positions [B, T] (Fast_dLLM_QwenRotaryEmbedding,
+        modeling.py:531-560: fp32 angles, cast to the model dtype)."""
+        f = pos.float()[..., None] * self.inv_freq[None, None, :]
+        emb = torch.cat((f, f), dim=-1)
+        return emb.cos().to(self.dtype), emb.sin().to(self.dtype)
+
+    @staticmethod
+    def apply_rope(x, cos, sin):
+        """x * cos + rotate_half(x) * sin on BSHD (modeling.py:186-199)."""
+        cos, sin = cos.unsqueeze(2), sin.unsqueeze(2)
+        h = x.shape[-1] // 2
+        return x * cos + torch.cat((-x[..., h:], x[..., :h]), dim=-1) * sin
+
+    def qkv(self, layer, x, cos, sin):
+        g = self.geo
+        B, T, _ = x.shape
+        y = torch.addmm(layer["bqkv"], x.view(B * T, -1), layer["wqkv"].t()).view(B, T, -1)
+        q = y[..., : g.heads * g.head_dim].view(B, T, g.heads, g.head_dim)
+        k = y[..., g.heads * g.head_dim: (g.heads + g.kv_heads) * g.head_dim].view(B, T, g.kv_heads, g.head_dim)
+        v = y[..., (g.heads + g.kv_heads) * g.head_dim:].view(B, T, g.kv_heads, g.head_dim)
+        return self.apply_rope(q, cos, sin).contiguous(), self.apply_rope(k, cos, sin).contiguous(), v.contiguous()
+
+    def mlp_residual(self, layer, h):
+        g = self.geo
+        B, T, _ = h.shape
+        x = self.rmsnorm(h, layer["ln2"])
+        gu = (x.view(B * T, -1) @ layer["wgu"].t()).view(B, T, 2 * g.ffn)
+        act = F.silu(gu[..., : g.ffn]) * gu[..., g.ffn:]
+        return h + (act.view(B * T, -1) @ layer["wd"].t()).view(B, T, -1)
+
+    def logits_rows(self, h_final_normed_rows):
+        return h_final_normed_rows @ self.lm_head.t()
+
+
+class DecodeState:
+    """Preallocated device state of one decode batch: committed KV cache
+    (BSHD per layer), dKV block buffers (BHSD per layer), sparse-prefix
+    buffers, per-sequence lengths and workspaces.  Nothing here is
+    reallocated while decoding, so every step is CUDA-graph capturable."""
+
+    def __init__(self, model: BlockDiffusionLM, batch: int, max_len: int, block: int = 32,
+                 sparse_keep: float | None = None):
+        g, dev, dt = model.geo, model.device, model.dtype
+        self.model, self.B, self.block, self.max_len = model, batch, block, max_len
+        self.k = [torch.zeros(batch, max_len, g.kv_heads, g.head_dim, dtype=dt, device=dev) for _ in range(g.layers)]
+        self.v = [torch.zeros_like(t) for t in self.k]
+        self.blk_k = [torch.zeros(batch, g.kv_heads, block, g.head_dim, dtype=dt, device=dev) for _ in range(g.layers)]
+        self.blk_v = [torch.zeros_like(t) for t in self.blk_k]
+        self.lens = torch.zeros(batch, dtype=torch.int32, device=dev)  # committed length per sequence
+        self.zero = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.sparse_keep = sparse_keep
+        if sparse_keep:
+            frac = sparse_keep.as_integer_ratio() if isinstance(sparse_keep, float) else (1, 4)
+            self.keep_num, self.keep_den = frac
+            self.max_keep = max(1, math.ceil(max_len * self.keep_num / self.keep_den))
+            self.sp_k = [torch.zeros(batch, self.max_keep, g.kv_heads, g.head_dim, dtype=dt, device=dev)
+                         for _ in range(g.layers)]
+            self.sp_v = [torch.zeros_like(t) for t in self.sp_k]
+            self.sp_len = [torch.zeros(batch, dtype=torch.int32, device=dev) for _ in range(g.layers)]
+            self.sp_sel = torch.empty(batch, self.max_keep, dtype=torch.int32, device=dev)
+            self.sp_ws = torch.empty(_lib.sparse_prefix_workspace_bytes(batch, max_len), dtype=torch.uint8,
+                                     device=dev)
+        ns = _lib.attn_auto_splits(batch, block, g.heads, g.kv_heads, max_len, block)
+        self.attn_splits = ns
+        wsb = _lib.attn_workspace_bytes(batch, max(block, 1), g.heads, ns)
+        self.attn_ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev) if wsb > 0 else None
+
+    # -------------------------------------------------------------- pieces
+    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos):
+        """Block attention for layer l: queries q [B, T, Hq, D] over the
+        committed prefix ("full") or the sparse prefix ("sparse") followed by
+        the given block K/V, under the block-causal mask."""
+        g = self.model.geo
+        out = torch.empty_like(q)
+        if prefix == "sparse":
+            kp, vp, lens = self.sp_k[l], self.sp_v[l], self.sp_len[l]
+        else:
+            kp, vp, lens = self.k[l], self.v[l], self.lens
+        T = q.shape[1]
+        ns = self.attn_splits if T <= self.block else _lib.attn_auto_splits(self.B, T, g.heads, g.kv_heads,
+                                                                            kp.shape[1], k_blk.shape[1])
+        ws = self.attn_ws
+        if ns > 1 and (ws is None or ws.numel() < _lib.attn_workspace_bytes(self.B, T, g.heads, ns)):
+            ws = torch.empty(_lib.attn_workspace_bytes(self.B, T, g.heads, ns), dtype=torch.uint8, device=q.device)
+        torch.ops.fdl.block_attn(q, kp, vp, lens, k_blk, v_blk, q_pos, self.block, g.head_dim ** -0.5, out,
+                                 ws if ns > 1 else None, ns)
+        return out
+
+    def select_sparse_prefix(self):
+        """Per layer: keep the top keep_num/keep_den committed prefix tokens by
+        key norm, gathered into the compact sparse-prefix buffers."""
+        for l in range(self.model.geo.layers):
+            torch.ops.fdl.kv_sparse_prefix(self.k[l], self.v[l], self.lens, self.keep_num, self.keep_den, self.sp_sel,
+                                           self.sp_len[l], self.sp_k[l], self.sp_v[l], self.sp_ws)
+
+    # ------------------------------------------------------------ forwards
+    def forward_commit(self, ids, pos):
+        """Forward over a fully decoded span (prompt prefill or a finished
+        block) that appends its K/V to the committed cache at self.lens and
+        attends over committed prefix + span (block-causal).  Returns the
+        final-normed hidden states of the span's last row [B, hidden]."""
+        m, g = self.model, self.model.geo
+        B, T = ids.shape
+        h = F.embedding(ids, m.embed)
+        cos, sin = m.rope(pos)
+        qpos = pos.to(torch.int32).contiguous()
+        for l, layer in enumerate(m.layers):
+            x = m.rmsnorm(h, layer["ln1"])
+            q, k, v = m.qkv(layer, x, cos, sin)
+            a = self.attend(q, l, "full", k, v, qpos)
+            torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
+            h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
+            h = m.mlp_residual(layer, h)
+        self.lens += T
+        return m.rmsnorm(h[:, -1:].contiguous(), m.norm)[:, 0]
+
+    def forward_block(self, ids, pos, fed=None, seed_hidden=None, prefix="full"):
+        """dKV diffusion step over the current block (forward_dkv,
+        modeling.py:1625-1692).  fed=None: full step, all block positions
+        recomputed and written to the block buffer (write_full); returns the
+        last-layer hidden [B, blk, hidden] (the seed for cached steps).  With
+        fed [B, n]: only those positions run; their K/V are scattered into the
+        block buffer and their outputs scattered onto seed_hidden."""
+        m = self.model
+        B = ids.shape[0]
+        if fed is None:
+            h = F.embedding(ids, m.embed)
+            p = pos
+        else:
+            h = F.embedding(torch.gather(ids, 1, fed), m.embed)
+            p = torch.gather(pos, 1, fed)
+        T = h.shape[1]
+        cos, sin = m.rope(p)
+        qpos = p.to(torch.int32).contiguous()
+        for l, layer in enumerate(m.layers):
+            x = m.rmsnorm(h, layer["ln1"])
+            q, k, v = m.qkv(layer, x, cos, sin)
+            bk, bv = self.blk_k[l], self.blk_v[l]
+            if fed is None:
+                torch.ops.fdl.kv_append([bk.transpose(1, 2)], [bv.transpose(1, 2)], [k], [v], self.zero)
+            else:
+                torch.ops.fdl.kv_scatter(bk, bv, k.transpose(1, 2), v.transpose(1, 2), fed, 2)
+            a = self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
+            h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
+            h = m.mlp_residual(layer, h)
+        if fed is None:
+            return h
+        out = seed_hidden.clone()
+        torch.ops.fdl.kv_scatter(out, None, h, None, fed, 1)
+        return out
+
+
+def dkv_fed_indices(prv_transfer_idx: torch.Tensor, width: int | None = None):
+    """_dkv_fed_indices (modeling.py:2039-2060) on the device: not-yet-frozen
+    positions in ascending order, padded (with the row's first fed index) to
+    the batch max -- or to `width` when given, so the step's shapes come
+    from a small fixed set."""
+    fed_mask = ~prv_transfer_idx
+    counts = fed_mask.sum(dim=1)
+    num = max(1, int(counts.max().item())) if width is None else width
+    order = torch.argsort(fed_mask.to(torch.int8), dim=1, descending=True, stable=True)
+    fed = order[:, :num].contiguous()
+    first = fed[:, :1]
+    slot = torch.arange(num, device=fed.device).unsqueeze(0)
+    pad = slot >= counts.clamp(min=1).unsqueeze(1)
+    return torch.where(pad, first.expand(-1, num), fed), num
+
+
+class BlockDiffusionDecoder:
+    """Greedy (temperature 0) block-diffusion decode of a batch with the dKV
+    schedule of batch_sample_dkv (generation_functions.py:2132-2340)."""
+
+    def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
+                 sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
+                 fed_bucket: int = 8, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID):
+        assert prompt_len % block == 0 and block % sub_block == 0
+        self.m, self.B, self.block, self.sub = model, batch, block, sub_block
+        self.threshold, self.refresh, self.fed_bucket = threshold, refresh, fed_bucket
+        self.mask_id, self.stop_id, self.pad_id = mask_id, stop_id, pad_id
+        self.prompt_len, self.gen_len = prompt_len, gen_len
+        max_len = prompt_len + gen_len + block
+        max_len = (max_len + 255) // 256 * 256
+        self.st = DecodeState(model, batch, max_len, block, sparse_keep)
+        self.prefix = "sparse" if sparse_keep else "full"
+        dev = model.device
+        self.ar = torch.arange(block, device=dev)
+        self.tokens = None
+
+    def prefill(self, prompt: torch.Tensor):
+        """Commit the prompt; returns the bridge token [B, 1]."""
+        B, P = prompt.shape
+        pos = torch.arange(P, device=prompt.device).unsqueeze(0).expand(B, -1)
+        self.st.lens.zero_()
+        hl = self.st.forward_commit(prompt, pos)
+        return self.m.logits_rows(hl).argmax(-1, keepdim=True)
+
+    def _sample(self, logits_rows, x_blk, s, e, finished):
+        """Threshold unmasking of sub-block [s, e) (generation_functions.py:2285-2305)."""
+        lf = logits_rows.float()
+        mx, x1 = lf.max(-1)
+        p = torch.exp(mx - torch.logsumexp(lf, -1))
+        mask_idx = x_blk[:, s:e] == self.mask_id
+        x1p = torch.where(mask_idx, p, torch.full_like(p, -math.inf))
+        unmask = x1p > self.threshold
+        unmask[torch.arange(x1.shape[0], device=x1.device), x1p.argmax(-1)] = True
+        unmask &= mask_idx
+        sub = x_blk[:, s:e]
+        x_blk[:, s:e] = torch.where(unmask, x1, sub)
+        finished |= ((x1 == self.stop_id) & unmask).any(dim=1)
+
+    def decode_block(self, bridge: torch.Tensor, finished: torch.Tensor, stats: dict | None = None):
+        """Decode one block: [bridge token, 31 masks] -> 32 tokens; commit;
+        returns (block tokens [B, 32], next bridge [B, 1])."""
+        m, st, blk = self.m, self.st, self.block
+        B = self.B
+        x = torch.full((B, blk), self.mask_id, dtype=torch.long, device=m.device)
+        x[:, :1] = bridge
+        x[finished] = self.pad_id
+        if self.prefix == "sparse":
+            st.select_sparse_prefix()
+        pos = st.lens.to(torch.long)[:, None] + self.ar[None, :]
+        prv = torch.zeros(B, blk, dtype=torch.bool, device=m.device)
+        cur = torch.zeros_like(prv)
+        seed = None
+        step_in_block = 0
+        n_fwd = 0
+        for sb in range(blk // self.sub):
+            s, e = sb * self.sub, (sb + 1) * self.sub
+            while True:
+                if not bool((x[:, s:e] == self.mask_id).any()):
+                    break
+                full = step_in_block <= 1 or step_in_block % self.refresh == 0
+                if full:
+                    seed = st.forward_block(x, pos, prefix=self.prefix)
+                    h = seed
+                else:
+                    fed_n = int((~prv).sum(1).max().item())
+                    width = min(blk, max(1, -(-fed_n // self.fed_bucket) * self.fed_bucket))
+                    fed, _ = dkv_fed_indices(prv, width)
+                    h = st.forward_block(x, pos, fed=fed, seed_hidden=seed, prefix=self.prefix)
+                n_fwd += 1
+                step_in_block += 1
+                # shifted logits: row i is predicted by position i-1 (row 0 by itself)
+                src = torch.clamp(torch.arange(s, e, device=m.device) - 1, min=0)
+                hn = m.rmsnorm(h[:, src].contiguous(), m.norm)
+                logits = m.logits_rows(hn)
+                self._sample(logits, x, s, e, finished)
+                prv, cur = cur, x != self.mask_id
+        hl = st.forward_commit(x, pos)
+        n_fwd += 1
+        nxt = m.logits_rows(hl).argmax(-1, keepdim=True)
+        nxt[finished] = self.pad_id
+        if stats is not None:
+            stats["forwards"] = stats.get("forwards", 0) + n_fwd
+        return x, nxt
+
+    def generate(self, prompt: torch.Tensor, n_blocks: int | None = None):
+        B = prompt.shape[0]
+        finished = torch.zeros(B, dtype=torch.bool, device=prompt.device)
+        bridge = self.prefill(prompt)
+        n_blocks = n_blocks if n_blocks is not None else self.gen_len // self.block
+        out = [prompt, bridge]
+        for _ in range(n_blocks):
+            blk, bridge = self.decode_block(bridge, finished)
+            out.append(blk[:, 1:])
+            out.append(bridge)
+        return torch.cat(out, dim=1), finished

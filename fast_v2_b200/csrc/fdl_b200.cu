@@ -292,7 +292,7 @@ int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb, const 
   a.B = batch; a.S = seq; a.T = n_tok; a.H = hidden;
   a.x_sb = x_sb * es; a.x_ss = x_ss * es; a.o_sb = out_sb * es; a.o_ss = out_ss * es;
   const uint64_t ptrs = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gathered) |
-                        reinterpret_cast<uintptr_t>(normed);
+                        reinterpret_cast<uintptr_t>(normed) | reinterpret_cast<uintptr_t>(w);
   const bool vec_ok = pick_vec({static_cast<uint64_t>(hidden) * es, ptrs, static_cast<uint64_t>(a.x_sb),
                                 static_cast<uint64_t>(a.x_ss), static_cast<uint64_t>(a.o_sb),
                                 static_cast<uint64_t>(a.o_ss)}) == 16;

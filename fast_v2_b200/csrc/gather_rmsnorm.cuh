@@ -93,17 +93,20 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
 
   char* gr = a.gathered ? a.gathered + b * a.o_sb + t * a.o_ss : nullptr;
   char* nr = a.normed + b * a.o_sb + t * a.o_ss;
-  const T* w = reinterpret_cast<const T*>(a.w);
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int vi = lane + 32 * k;
     if (vi < nvec) {
       if (gr) st_stream16(gr + vi * 16, v[k]);
       const T* e = reinterpret_cast<const T*>(&v[k]);
+      // One 16-byte weight load per vector (L1/L2 resident across rows).
+      uint4 wv;
+      if (a.w) wv = *reinterpret_cast<const uint4*>(a.w + vi * 16);
+      const T* we = reinterpret_cast<const T*>(&wv);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int j = 0; j < EPV; ++j) oe[j] = norm_elem<T>(ElemOps<T>::to_f(e[j]), inv, w, vi * EPV + j);
+      for (int j = 0; j < EPV; ++j) oe[j] = norm_elem<T>(ElemOps<T>::to_f(e[j]), inv, a.w ? we : nullptr, j);
       st_stream16(nr + vi * 16, o);
     }
   }
