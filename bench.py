@@ -15,6 +15,11 @@ Configs (BASELINE.json `configs`):
                 GQA-7 expansion, cache [16, 4096, 4, 128] per layer and K/V
   block_attn    block attention Q [B, 32, 28, 128] over a prefix of P keys
                 (--attn-b, --attn-p, --attn-sq select the point)
+  e2e_7b        (default) block-diffusion decode at Qwen2.5-7B geometry,
+                random init, 64 sequences/GPU, prompt 1024, dKV block cache
+                + token-sparse prefix; one step = one 32-token block
+  e2e_1_5b      the same at Qwen2.5-1.5B geometry, 16 sequences, prompt 256,
+                static cache (full block recompute every step)
 
 Inputs are seeded synthetic tensors (the reference's datasets and weights are
 not available offline).  Between timed steps the inputs rotate through buffer
@@ -137,7 +142,7 @@ def setup_dist():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    else:
+    elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return world, rank, local
 
@@ -365,8 +370,148 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
         dtype="bf16", cpu_sample=cpu_sample)
 
 
-WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn}
-DEFAULT_CONFIG = "kv_path"
+_CPU_CACHE = {}
+
+
+def _cpu_time(layers, pk, pv, emb, ids, geod, past, nl):
+    from oracle import torch_port
+
+    dt = emb.dtype
+    t0 = time.perf_counter()
+    torch_port.dkv_full_step_forward(layers, emb[:1024], torch.ones(geod["hidden"], dtype=dt), emb[:1024], ids, pk,
+                                     pv, past, geod)
+    t_layers = (time.perf_counter() - t0) / nl * geod["layers"]
+    x = torch.randn(8, geod["hidden"]).to(dt)
+    t1 = time.perf_counter()
+    torch.nn.functional.linear(x, emb)
+    t_fwd = t_layers + (time.perf_counter() - t1)
+    return 1.0 / t_fwd, (f"1 sequence x 1 full dKV step of the reference torch path: {nl} of {geod['layers']} "
+                         f"layers timed and scaled, lm_head on 8 rows; 1 generated token per forward")
+
+
+def _e2e(args, rank, world, kt, geo_name):
+    from fast_v2_b200.block_decode import QWEN25_1_5B, QWEN25_7B, BlockDiffusionDecoder, BlockDiffusionLM, param_count
+
+    if geo_name == "7b":
+        geo, B, P, G, sparse, refresh = QWEN25_7B, 64, 1024, 1024, 0.25, 4
+        cache_desc = "dynamic block KV (dKV, refresh 4) + token-sparse prefix (top 25% by key norm, per block)"
+    else:
+        geo, B, P, G, sparse, refresh = QWEN25_1_5B, 16, 256, 512, None, 1
+        cache_desc = "static KV cache, full block recompute every step"
+    B = args.e2e_batch or B
+    cpu_only = getattr(args, "impl", "ours") == "reference"
+    model = None if cpu_only else BlockDiffusionLM(geo, device="cuda", seed=100 + rank)
+    meta = dict(
+        metric=f"generated tokens/s ({geo_name.upper()} geometry, bs{B}/GPU, block-diffusion decode)",
+        unit="tokens/s", dtype="bf16",
+        config={"workload": f"e2e_{geo_name}", "model": f"Qwen2.5-{geo_name.upper()} geometry, random init",
+                "params": param_count(geo), "batch_per_gpu": B, "prompt": P, "gen": G, "block": 32, "sub_block": 8,
+                "threshold": 0.9, "cache": cache_desc, "step": "one 32-token block (diffusion steps + commit)",
+                "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
+    dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
+                                                      use_graphs=True)
+    g = gen(4000 + rank)
+    if not cpu_only:
+        prompt = torch.randint(0, 151643, (B, P), generator=g).cuda()
+        max_blocks = G // 32
+        if args.warmup + args.steps + 2 > max_blocks:
+            raise SystemExit(f"--warmup + --steps must be <= {max_blocks - 2} blocks for this config")
+        with torch.no_grad():
+            state = {"bridge": dec.prefill(prompt)}
+            dec.capture_all()
+        torch.cuda.synchronize()
+        stats = {}
+
+        def step():
+            with torch.no_grad():
+                _, state["bridge"] = dec.decode_block(state["bridge"], stats=stats)
+
+        # e2e: the host-facing call per block -- bridge token in from pinned host
+        # memory, the block's 32 tokens back to pinned host memory.
+        hb = torch.empty(B, 1, dtype=torch.long).pin_memory()
+        hblk = torch.empty(B, 32, dtype=torch.long).pin_memory()
+
+        def e2e_step():
+            with torch.no_grad():
+                hb.copy_(state["bridge"], non_blocking=True)
+                bridge = hb.to("cuda", non_blocking=True)
+                blk, state["bridge"] = dec.decode_block(bridge, stats=stats)
+                hblk.copy_(blk, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        # dominant kernel of ours in the step: the block attention of a full
+        # diffusion step (layer 0, current prefix state)
+        st = dec.st
+        q = (torch.randn(B, 32, geo.heads, geo.head_dim, device="cuda") * 0.1).to(torch.bfloat16)
+        kb, vb = st.blk_k[0].transpose(1, 2), st.blk_v[0].transpose(1, 2)
+        qpos = dec.pos.to(torch.int32)
+
+        def dominant():
+            st.attend(q, 0, dec.prefix, kb, vb, qpos)
+
+        def dom_work():
+            lens = float((st.sp_len[0] if sparse else st.lens).float().mean().item())
+            kv = B * (lens + 32) * geo.kv_heads * geo.head_dim * 2 * 2
+            flops = 4 * B * geo.heads * 32 * (lens + 32) * geo.head_dim
+            return kv, flops
+
+    def cpu_sample():
+        """The reference's full dKV step on the host CPU for ONE sequence at this
+        geometry (oracle/torch_port.dkv_full_step_forward): 2 layers timed and
+        scaled to all layers, plus the lm_head rows; with random weights one
+        token is committed per forward, so tokens/s = 1 / forward time."""
+        from oracle import torch_port
+
+        gg = torch.Generator().manual_seed(7)
+        D, dt = geo.head_dim, torch.bfloat16
+
+        def rnd(*shape):
+            return torch.empty(*shape, dtype=dt).normal_(0.0, 0.02, generator=gg)
+
+        nl = 2
+        if "cpu" in _CPU_CACHE:
+            layers, pk, pv, emb, ids, geod, past = _CPU_CACHE["cpu"]
+            return _cpu_time(layers, pk, pv, emb, ids, geod, past, nl)
+        layers = [dict(wq=rnd(geo.heads * D, geo.hidden), bq=torch.zeros(geo.heads * D, dtype=dt),
+                       wk=rnd(geo.kv_heads * D, geo.hidden), bk=torch.zeros(geo.kv_heads * D, dtype=dt),
+                       wv=rnd(geo.kv_heads * D, geo.hidden), bv=torch.zeros(geo.kv_heads * D, dtype=dt),
+                       wo=rnd(geo.hidden, geo.heads * D), ln1=torch.ones(geo.hidden, dtype=dt),
+                       ln2=torch.ones(geo.hidden, dtype=dt), wg=rnd(geo.ffn, geo.hidden), wu=rnd(geo.ffn, geo.hidden),
+                       wd=rnd(geo.hidden, geo.ffn)) for _ in range(nl)]
+        past = P + 64
+        pl = int(math.ceil(0.25 * past)) if sparse else past
+        pk = [rnd(1, geo.kv_heads, pl, D) for _ in range(nl)]
+        pv = [rnd(1, geo.kv_heads, pl, D) for _ in range(nl)]
+        emb = rnd(geo.vocab, geo.hidden)
+        ids = torch.randint(0, 1000, (1, 32), generator=gg)
+        geod = dict(head_dim=D, heads=geo.heads, kv_heads=geo.kv_heads, rope_theta=geo.rope_theta, eps=geo.eps,
+                    layers=geo.layers, hidden=geo.hidden)
+        _CPU_CACHE["cpu"] = (layers, pk, pv, emb, ids, geod, past)
+        torch_port.dkv_full_step_forward(layers[:1], emb[:1024], torch.ones(geo.hidden, dtype=dt), emb[:1024], ids,
+                                         pk, pv, past, geod)  # warm-up
+        return _cpu_time(layers, pk, pv, emb, ids, geod, past, nl)
+
+    if cpu_only:
+        return dict(meta, cpu_sample=cpu_sample)
+    kvb, fl = dom_work()
+    return dict(meta, units_per_step=B * 32, step=step, dominant=dominant, graph=False, e2e_step=e2e_step,
+                e2e_bytes=(B * 8, B * 32 * 8),
+                roofline=dict(bound="hbm", per_launch=kvb, kernel="block_attn_kernel (full dKV step, layer 0)",
+                              flops=fl, dynamic=dom_work),
+                launches_per_step=None, stats=stats, cpu_sample=cpu_sample)
+
+
+def wl_e2e_7b(args, rank, world, kt):
+    return _e2e(args, rank, world, kt, "7b")
+
+
+def wl_e2e_1_5b(args, rank, world, kt):
+    return _e2e(args, rank, world, kt, "1.5b")
+
+
+WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn,
+             "e2e_7b": wl_e2e_7b, "e2e_1_5b": wl_e2e_1_5b}
+DEFAULT_CONFIG = "e2e_7b"
 
 
 # --------------------------------------------------------------------------
@@ -389,7 +534,7 @@ def run_reference(args, world, rank):
     import types
 
     fake_args = types.SimpleNamespace(**vars(args))
-    if not torch.cuda.is_available():
+    if not torch.cuda.is_available() and not args.config.startswith("e2e"):
         raise SystemExit(json.dumps({"impl": "reference", "unavailable": "needs the GPU box to stage inputs"}))
     w = WORKLOADS[args.config](fake_args, 0, 1, _Noop())
     vals = []
@@ -424,10 +569,11 @@ def main():
     ap.add_argument("--attn-b", type=int, default=64)
     ap.add_argument("--attn-p", type=int, default=8192)
     ap.add_argument("--attn-sq", type=int, default=32)
+    ap.add_argument("--e2e-batch", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"gather_norm": 2000, "kv_path": 100, "block_attn": 200}.get(args.config, 20)
+        args.steps = {"gather_norm": 2000, "kv_path": 100, "block_attn": 200}.get(args.config, 8)
     args.warmup = max(3, args.warmup)
     world, rank, local = setup_dist()
 
@@ -460,6 +606,8 @@ def main():
     sampler.start()
     barrier(world)
     kt.active = not w.get("graph")
+    from fast_v2_b200 import _lib as _fdl_lib
+    launches0 = _fdl_lib.launches
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
     start.record(stream)
@@ -472,6 +620,7 @@ def main():
     torch.cuda.synchronize()
     t1 = time.time()
     kt.active = False
+    launches_timed = _fdl_lib.launches - launches0
     sampler.mark(t0, t1)
     barrier(world)
     sampler.stop()
@@ -502,6 +651,8 @@ def main():
     else:
         kms = kt.avg_ms()
     roof = None
+    if rf.get("dynamic"):
+        rf["per_launch"], rf["flops"] = rf["dynamic"]()
     if kms:
         if rf["bound"] == "hbm":
             ach = rf["per_launch"] / (kms / 1e3) / 1e9
@@ -509,6 +660,8 @@ def main():
             roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"],
                     "launch_us": round(kms * 1e3, 2), "peak_src": peaks["src"]}
+            if rf.get("flops"):
+                roof["tflops_achieved"] = round(rf["flops"] / (kms / 1e3) / 1e12, 1)
         else:
             ach = rf["per_launch"] / (kms / 1e3) / 1e12
             peak = peaks["bf16_tflops"]
@@ -553,7 +706,8 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
             "config": {**w["config"], "parallelism": f"dp{world} (sequence-sharded replicas)"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": sampler.summary(),
-            "gpu_launches": w["launches_per_step"] * args.steps,
+            "gpu_launches": (w["launches_per_step"] * args.steps if w["launches_per_step"] is not None
+                             else launches_timed),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -33,6 +33,15 @@ EXPORTS = (
 )
 
 _lock = threading.Lock()
+# Host-side tally of fdl kernel launches issued by the Python drivers (a CUDA
+# graph replay adds the count recorded at its capture); bench.py reports it.
+launches = 0
+
+
+def count_launches(n: int = 1) -> None:
+    global launches
+    launches += n
+
 _abi: ctypes.CDLL | None = None
 _ops_loaded = False
 

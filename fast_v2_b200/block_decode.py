@@ -26,7 +26,7 @@ The decode loop follows the reference's dKV sampler ``batch_sample_dkv``
 * block complete: commit forward over the 32 final tokens appends their K/V
   to the committed cache; its last logit gives the next bridge token.
 
-``sparse_prefix`` (a keep fraction, e.g. 0.25) replaces the committed prefix
+``sparse_keep`` (a keep fraction, e.g. 0.25) replaces the committed prefix
 seen by the diffusion steps with the top-scoring prefix tokens by key norm,
 re-selected once per block (no reference counterpart; see
 include/fdl_kvcache.h, fdl_kv_sparse_prefix).
@@ -81,8 +81,9 @@ class BlockDiffusionLM:
     modeling.py:511-522).  q/k/v and gate/up projections are stored fused."""
 
     def __init__(self, geo: Geometry, device="cuda", dtype=torch.bfloat16, seed: int = 0, init_std: float = 0.02,
-                 init_device: str | None = None):
-        _lib.ensure_ops()
+                 init_device: str | None = None, load_ops: bool = True):
+        if load_ops:
+            _lib.ensure_ops()
         self.geo, self.device, self.dtype = geo, torch.device(device), dtype
         g = geo
         # Generation on the target device is fast; init_device="cpu" gives
@@ -116,11 +117,12 @@ class BlockDiffusionLM:
     def rmsnorm(self, x, w):
         out = torch.empty_like(x)
         torch.ops.fdl.gather_rmsnorm(x, None, w, self.geo.eps, None, out)
+        _lib.count_launches(1)
         return out
 
     def rope(self, pos):
         """cos/sin [B, T, D] for integer positions [B, T] (Fast_dLLM_QwenRotaryEmbedding,
-        modeling.py:531-560: fp32 angles, cast to the model dtype)."""
+        modeling.py:545-560: fp32 angles, cast to the model dtype)."""
         f = pos.float()[..., None] * self.inv_freq[None, None, :]
         emb = torch.cat((f, f), dim=-1)
         return emb.cos().to(self.dtype), emb.sin().to(self.dtype)
@@ -171,8 +173,7 @@ class DecodeState:
         self.zero = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.sparse_keep = sparse_keep
         if sparse_keep:
-            frac = sparse_keep.as_integer_ratio() if isinstance(sparse_keep, float) else (1, 4)
-            self.keep_num, self.keep_den = frac
+            self.keep_num, self.keep_den = float(sparse_keep).as_integer_ratio()
             self.max_keep = max(1, math.ceil(max_len * self.keep_num / self.keep_den))
             self.sp_k = [torch.zeros(batch, self.max_keep, g.kv_heads, g.head_dim, dtype=dt, device=dev)
                          for _ in range(g.layers)]
@@ -183,7 +184,7 @@ class DecodeState:
                                      device=dev)
         ns = _lib.attn_auto_splits(batch, block, g.heads, g.kv_heads, max_len, block)
         self.attn_splits = ns
-        wsb = _lib.attn_workspace_bytes(batch, max(block, 1), g.heads, ns)
+        wsb = _lib.attn_workspace_bytes(batch, block, g.heads, ns)
         self.attn_ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev) if wsb > 0 else None
 
     # -------------------------------------------------------------- pieces
@@ -205,6 +206,7 @@ class DecodeState:
             ws = torch.empty(_lib.attn_workspace_bytes(self.B, T, g.heads, ns), dtype=torch.uint8, device=q.device)
         torch.ops.fdl.block_attn(q, kp, vp, lens, k_blk, v_blk, q_pos, self.block, g.head_dim ** -0.5, out,
                                  ws if ns > 1 else None, ns)
+        _lib.count_launches(2 if ns > 1 else 1)
         return out
 
     def select_sparse_prefix(self):
@@ -213,14 +215,16 @@ class DecodeState:
         for l in range(self.model.geo.layers):
             torch.ops.fdl.kv_sparse_prefix(self.k[l], self.v[l], self.lens, self.keep_num, self.keep_den, self.sp_sel,
                                            self.sp_len[l], self.sp_k[l], self.sp_v[l], self.sp_ws)
+            _lib.count_launches(3)
 
     # ------------------------------------------------------------ forwards
-    def forward_commit(self, ids, pos):
+    def forward_commit(self, ids, pos, all_rows: bool = False):
         """Forward over a fully decoded span (prompt prefill or a finished
         block) that appends its K/V to the committed cache at self.lens and
         attends over committed prefix + span (block-causal).  Returns the
-        final-normed hidden states of the span's last row [B, hidden]."""
-        m, g = self.model, self.model.geo
+        final-normed hidden state of the span's last row [B, hidden] (all rows
+        [B, T, hidden] with all_rows=True)."""
+        m = self.model
         B, T = ids.shape
         h = F.embedding(ids, m.embed)
         cos, sin = m.rope(pos)
@@ -230,9 +234,12 @@ class DecodeState:
             q, k, v = m.qkv(layer, x, cos, sin)
             a = self.attend(q, l, "full", k, v, qpos)
             torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
+            _lib.count_launches(1)
             h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
             h = m.mlp_residual(layer, h)
         self.lens += T
+        if all_rows:
+            return m.rmsnorm(h, m.norm)
         return m.rmsnorm(h[:, -1:].contiguous(), m.norm)[:, 0]
 
     def forward_block(self, ids, pos, fed=None, seed_hidden=None, prefix="full"):
@@ -261,6 +268,7 @@ class DecodeState:
                 torch.ops.fdl.kv_append([bk.transpose(1, 2)], [bv.transpose(1, 2)], [k], [v], self.zero)
             else:
                 torch.ops.fdl.kv_scatter(bk, bv, k.transpose(1, 2), v.transpose(1, 2), fed, 2)
+            _lib.count_launches(1)
             a = self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
             h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
             h = m.mlp_residual(layer, h)
@@ -268,6 +276,7 @@ class DecodeState:
             return h
         out = seed_hidden.clone()
         torch.ops.fdl.kv_scatter(out, None, h, None, fed, 1)
+        _lib.count_launches(1)
         return out
 
 
@@ -289,11 +298,19 @@ def dkv_fed_indices(prv_transfer_idx: torch.Tensor, width: int | None = None):
 
 class BlockDiffusionDecoder:
     """Greedy (temperature 0) block-diffusion decode of a batch with the dKV
-    schedule of batch_sample_dkv (generation_functions.py:2132-2340)."""
+    schedule of batch_sample_dkv (generation_functions.py:2132-2340).
+
+    Every diffusion step works on static device buffers (block tokens,
+    positions, sub-block index, frozen masks, seed hidden states), so with
+    ``use_graphs=True`` each step is one CUDA-graph replay: one graph for the
+    full-block step and one per bucketed width of the cached step.  The host
+    reads two scalars per step (any masks left in the sub-block; the fed
+    width), as the reference's loop does."""
 
     def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
                  sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
-                 fed_bucket: int = 8, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID):
+                 fed_bucket: int = 8, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
+                 use_graphs: bool = False):
         assert prompt_len % block == 0 and block % sub_block == 0
         self.m, self.B, self.block, self.sub = model, batch, block, sub_block
         self.threshold, self.refresh, self.fed_bucket = threshold, refresh, fed_bucket
@@ -305,84 +322,155 @@ class BlockDiffusionDecoder:
         self.prefix = "sparse" if sparse_keep else "full"
         dev = model.device
         self.ar = torch.arange(block, device=dev)
-        self.tokens = None
+        B, H = batch, model.geo.hidden
+        self.x = torch.full((B, block), mask_id, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(B, block, dtype=torch.long, device=dev)
+        self.prv = torch.zeros(B, block, dtype=torch.bool, device=dev)
+        self.cur = torch.zeros(B, block, dtype=torch.bool, device=dev)
+        self.seed = torch.zeros(B, block, H, dtype=model.dtype, device=dev)
+        self.finished = torch.zeros(B, dtype=torch.bool, device=dev)
+        self.sub_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
+        self.src_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
+        self._subs = [torch.arange(s, s + sub_block, device=dev) for s in range(0, block, sub_block)]
+        self._srcs = [torch.clamp(t - 1, min=0) for t in self._subs]
+        self.use_graphs = use_graphs
+        self._graphs = {}
+        self._graph_launches = {}
+        self._pool = None
 
+    # ------------------------------------------------------------- steps
+    def _sample(self, h):
+        """Threshold unmasking of the current sub-block (generation_functions.py:
+        2285-2305) from the last-layer hidden states h [B, block, hidden].
+        Logits only for the rows the sampler reads: row i of the sub-block is
+        predicted by position i-1 (row 0 by itself).  As sample_with_top_p at
+        temperature 0 (modeling.py:2263-2269): softmax in the logits dtype,
+        argmax = first maximal probability."""
+        m = self.m
+        hn = m.rmsnorm(h.index_select(1, self.src_idx).contiguous(), m.norm)
+        p, x1 = torch.softmax(m.logits_rows(hn), dim=-1).max(-1)
+        sub = self.x.index_select(1, self.sub_idx)
+        mask_idx = sub == self.mask_id
+        x1p = torch.where(mask_idx, p, torch.full_like(p, -math.inf))
+        unmask = x1p > self.threshold
+        unmask.scatter_(1, x1p.argmax(-1, keepdim=True), True)
+        unmask &= mask_idx
+        self.x.index_copy_(1, self.sub_idx, torch.where(unmask, x1, sub))
+        self.finished |= ((x1 == self.stop_id) & unmask).any(dim=1)
+        self.prv.copy_(self.cur)
+        self.cur.copy_(self.x != self.mask_id)
+
+    def _full_step(self):
+        h = self.st.forward_block(self.x, self.pos, prefix=self.prefix)
+        self.seed.copy_(h)
+        self._sample(self.seed)
+
+    def _cached_step(self, width):
+        fed, _ = dkv_fed_indices(self.prv, width)
+        h = self.st.forward_block(self.x, self.pos, fed=fed, seed_hidden=self.seed, prefix=self.prefix)
+        self._sample(h)
+
+    def _step_fn(self, key):
+        return self._full_step if key == "full" else (lambda: self._cached_step(key))
+
+    def _capture(self, key):
+        """Capture the step `key` ("full" or a cached width) into a CUDA graph.
+        A warm-up run on a side stream precedes capture; every static buffer it
+        touches is restored afterwards (the block buffers it rewrites are
+        rewritten by the first full step of every block anyway)."""
+        fn = self._step_fn(key)
+        bufs = (self.x, self.prv, self.cur, self.seed, self.finished)
+        snap = [t.clone() for t in bufs]
+        n0 = _lib.launches
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        for t, v in zip(bufs, snap):
+            t.copy_(v)
+        g = torch.cuda.CUDAGraph()
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        n1 = _lib.launches
+        with torch.cuda.graph(g, pool=self._pool):
+            fn()
+        self._graph_launches[key] = _lib.launches - n1
+        _lib.launches = n0
+        for t, v in zip(bufs, snap):
+            t.copy_(v)
+        self._graphs[key] = g
+        return g
+
+    def capture_all(self):
+        """Capture every step variant up front (full step and cached widths)."""
+        if not self.use_graphs:
+            return
+        for key in ["full"] + list(range(self.fed_bucket, self.block + 1, self.fed_bucket)):
+            if key not in self._graphs:
+                self._capture(key)
+        torch.cuda.synchronize()
+
+    def _run(self, key):
+        if not self.use_graphs:
+            self._step_fn(key)()
+            return
+        g = self._graphs.get(key) or self._capture(key)
+        g.replay()
+        _lib.count_launches(self._graph_launches[key])
+
+    # ------------------------------------------------------------- public
     def prefill(self, prompt: torch.Tensor):
         """Commit the prompt; returns the bridge token [B, 1]."""
         B, P = prompt.shape
         pos = torch.arange(P, device=prompt.device).unsqueeze(0).expand(B, -1)
         self.st.lens.zero_()
+        self.finished.zero_()
         hl = self.st.forward_commit(prompt, pos)
         return self.m.logits_rows(hl).argmax(-1, keepdim=True)
 
-    def _sample(self, logits_rows, x_blk, s, e, finished):
-        """Threshold unmasking of sub-block [s, e) (generation_functions.py:2285-2305)."""
-        lf = logits_rows.float()
-        mx, x1 = lf.max(-1)
-        p = torch.exp(mx - torch.logsumexp(lf, -1))
-        mask_idx = x_blk[:, s:e] == self.mask_id
-        x1p = torch.where(mask_idx, p, torch.full_like(p, -math.inf))
-        unmask = x1p > self.threshold
-        unmask[torch.arange(x1.shape[0], device=x1.device), x1p.argmax(-1)] = True
-        unmask &= mask_idx
-        sub = x_blk[:, s:e]
-        x_blk[:, s:e] = torch.where(unmask, x1, sub)
-        finished |= ((x1 == self.stop_id) & unmask).any(dim=1)
-
-    def decode_block(self, bridge: torch.Tensor, finished: torch.Tensor, stats: dict | None = None):
+    def decode_block(self, bridge: torch.Tensor, stats: dict | None = None):
         """Decode one block: [bridge token, 31 masks] -> 32 tokens; commit;
         returns (block tokens [B, 32], next bridge [B, 1])."""
         m, st, blk = self.m, self.st, self.block
-        B = self.B
-        x = torch.full((B, blk), self.mask_id, dtype=torch.long, device=m.device)
-        x[:, :1] = bridge
-        x[finished] = self.pad_id
+        self.x.fill_(self.mask_id)
+        self.x[:, :1] = bridge
+        self.x.masked_fill_(self.finished[:, None], self.pad_id)
         if self.prefix == "sparse":
             st.select_sparse_prefix()
-        pos = st.lens.to(torch.long)[:, None] + self.ar[None, :]
-        prv = torch.zeros(B, blk, dtype=torch.bool, device=m.device)
-        cur = torch.zeros_like(prv)
-        seed = None
+        self.pos.copy_(st.lens.to(torch.long)[:, None] + self.ar[None, :])
+        self.prv.zero_()
+        self.cur.zero_()
         step_in_block = 0
         n_fwd = 0
         for sb in range(blk // self.sub):
+            self.sub_idx.copy_(self._subs[sb])
+            self.src_idx.copy_(self._srcs[sb])
             s, e = sb * self.sub, (sb + 1) * self.sub
-            while True:
-                if not bool((x[:, s:e] == self.mask_id).any()):
-                    break
-                full = step_in_block <= 1 or step_in_block % self.refresh == 0
-                if full:
-                    seed = st.forward_block(x, pos, prefix=self.prefix)
-                    h = seed
+            while bool((self.x[:, s:e] == self.mask_id).any()):
+                if step_in_block <= 1 or step_in_block % self.refresh == 0:
+                    self._run("full")
                 else:
-                    fed_n = int((~prv).sum(1).max().item())
-                    width = min(blk, max(1, -(-fed_n // self.fed_bucket) * self.fed_bucket))
-                    fed, _ = dkv_fed_indices(prv, width)
-                    h = st.forward_block(x, pos, fed=fed, seed_hidden=seed, prefix=self.prefix)
+                    fed_n = int((~self.prv).sum(1).max().item())
+                    self._run(min(blk, max(1, -(-fed_n // self.fed_bucket) * self.fed_bucket)))
                 n_fwd += 1
                 step_in_block += 1
-                # shifted logits: row i is predicted by position i-1 (row 0 by itself)
-                src = torch.clamp(torch.arange(s, e, device=m.device) - 1, min=0)
-                hn = m.rmsnorm(h[:, src].contiguous(), m.norm)
-                logits = m.logits_rows(hn)
-                self._sample(logits, x, s, e, finished)
-                prv, cur = cur, x != self.mask_id
-        hl = st.forward_commit(x, pos)
+        x = self.x.clone()
+        hl = st.forward_commit(x, self.pos)
         n_fwd += 1
         nxt = m.logits_rows(hl).argmax(-1, keepdim=True)
-        nxt[finished] = self.pad_id
+        nxt[self.finished] = self.pad_id
         if stats is not None:
             stats["forwards"] = stats.get("forwards", 0) + n_fwd
+            stats["blocks"] = stats.get("blocks", 0) + 1
         return x, nxt
 
     def generate(self, prompt: torch.Tensor, n_blocks: int | None = None):
-        B = prompt.shape[0]
-        finished = torch.zeros(B, dtype=torch.bool, device=prompt.device)
         bridge = self.prefill(prompt)
         n_blocks = n_blocks if n_blocks is not None else self.gen_len // self.block
         out = [prompt, bridge]
         for _ in range(n_blocks):
-            blk, bridge = self.decode_block(bridge, finished)
+            blk, bridge = self.decode_block(bridge)
             out.append(blk[:, 1:])
             out.append(bridge)
-        return torch.cat(out, dim=1), finished
+        return torch.cat(out, dim=1), self.finished.clone()

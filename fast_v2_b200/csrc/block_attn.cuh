@@ -296,10 +296,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     const int q = q0 + sq_i;
     const int head = g * p.G + (r - sq_i * p.G);
     const bool valid_row = (r < R) && (q < p.Sq);
-    int qblk = 0;
+    // Block-causal mask as a key-position bound: key position kp is visible
+    // iff kp / mask_block <= qpos / mask_block, i.e. kp < kpos_end.
+    int kpos_end = 0x7fffffff;
     if (p.mask_block > 0 && valid_row) {
       const int qpos = p.q_pos ? p.q_pos[static_cast<int64_t>(b) * p.Sq + q] : len + q;
-      qblk = qpos / p.mask_block;
+      kpos_end = (qpos / p.mask_block + 1) * p.mask_block;
     }
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tmem + lane_off + kTmemS + m * kBlockN;
@@ -320,12 +322,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       if (lane == 0) ptx::mbar_arrive(&bars->s_empty[m]);
 
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+      // Visible keys of this tile for this row form a prefix of the tile, so
+      // the mask is one compare per element (no division in the loop).
+      const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : 0;
       float tmax = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        bool allowed = valid_row && c < ti.valid;
-        if (p.mask_block > 0) allowed = allowed && (qblk >= (ti.kpos0 + c) / p.mask_block);
-        s[c] = allowed ? s[c] * p.scale_log2 : -INFINITY;
+        s[c] = c < climit ? s[c] * p.scale_log2 : -INFINITY;
         tmax = fmaxf(tmax, s[c]);
       }
       const float m_new = fmaxf(m_used, tmax);

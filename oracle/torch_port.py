@@ -79,3 +79,59 @@ def flash_kvcache_sdpa(query, k_cache, v_cache, cache_seqlens, scaling=None):
     attn_mask.masked_fill_(~valid[:, None, None, :], float("-inf"))
     out = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask, scale=scale)
     return out.transpose(1, 2).contiguous()
+
+
+def rmsnorm(x, w, eps):
+    """Fast_dLLM_QwenRMSNorm.forward (modeling.py:427-432)."""
+    dt = x.dtype
+    h = x.to(torch.float32)
+    var = h.pow(2).mean(-1, keepdim=True)
+    return w * (h * torch.rsqrt(var + eps)).to(dt)
+
+
+def rope(x_bhsd, cos, sin):
+    """apply_rotary_pos_emb (modeling.py:186-199), BHSD with cos/sin [1, S, D]."""
+    cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+    h = x_bhsd.shape[-1] // 2
+    rot = torch.cat((-x_bhsd[..., h:], x_bhsd[..., :h]), dim=-1)
+    return x_bhsd * cos + rot * sin
+
+
+def dkv_full_step_forward(layers, embed, norm_w, lm_head, ids, prefix_k, prefix_v, past_len, geo):
+    """One full dKV diffusion step of the reference on CPU (forward_dkv with
+    is_full_step=True, modeling.py:1625-1662, through Fast_dLLM_QwenDecoderLayer
+    and Fast_dLLM_QwenAttention.forward with dkv_store, modeling.py:327-415):
+    embed -> per layer [RMSNorm, q/k/v, RoPE, cat(prefix, block), repeat_kv +
+    SDPA under eval_mask, o_proj, residual, RMSNorm, SwiGLU MLP, residual] ->
+    norm -> lm_head.  `layers` holds per-layer dicts of torch weights
+    (wq, bq, wk, bk, wv, bv, wo, ln1, ln2, wg, wu, wd); prefix_k/v are
+    per-layer BHSD [B, Hkv, P, D]."""
+    B, T = ids.shape
+    D, Hq, Hkv = geo["head_dim"], geo["heads"], geo["kv_heads"]
+    h = F.embedding(ids, embed)
+    pos = torch.arange(past_len, past_len + T, dtype=torch.float32)
+    inv = 1.0 / (geo["rope_theta"] ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))
+    f = pos[:, None] * inv[None, :]
+    emb = torch.cat((f, f), dim=-1)
+    cos, sin = emb.cos().to(h.dtype)[None], emb.sin().to(h.dtype)[None]
+    qi = torch.arange(T)[:, None] + past_len
+    kj = torch.arange(T + prefix_k[0].shape[2])[None, :]
+    mask = (qi // 32) >= (kj // 32)
+    for l, w in enumerate(layers):
+        res = h
+        x = rmsnorm(h, w["ln1"], geo["eps"])
+        q = F.linear(x, w["wq"], w["bq"]).view(B, T, Hq, D).transpose(1, 2)
+        k = F.linear(x, w["wk"], w["bk"]).view(B, T, Hkv, D).transpose(1, 2)
+        v = F.linear(x, w["wv"], w["bv"]).view(B, T, Hkv, D).transpose(1, 2)
+        q, k = rope(q, cos, sin), rope(k, cos, sin)
+        fk = torch.cat((prefix_k[l], k), dim=-2)
+        fv = torch.cat((prefix_v[l], v), dim=-2)
+        n_rep = Hq // Hkv
+        fk = fk[:, :, None].expand(-1, -1, n_rep, -1, -1).reshape(B, Hq, -1, D)
+        fv = fv[:, :, None].expand(-1, -1, n_rep, -1, -1).reshape(B, Hq, -1, D)
+        a = F.scaled_dot_product_attention(q, fk, fv, attn_mask=mask, scale=D ** -0.5)
+        h = res + F.linear(a.transpose(1, 2).reshape(B, T, Hq * D), w["wo"])
+        x = rmsnorm(h, w["ln2"], geo["eps"])
+        h = h + F.linear(F.silu(F.linear(x, w["wg"])) * F.linear(x, w["wu"]), w["wd"])
+    h = rmsnorm(h, norm_w, geo["eps"])
+    return F.linear(h, lm_head)
