@@ -24,6 +24,7 @@ EXPORTS = (
     "fdl_kv_gather_rows",
     "fdl_sparse_prefix_workspace_bytes",
     "fdl_kv_sparse_prefix",
+    "fdl_kv_sparse_prefix_noalloc",
     "fdl_gather_rmsnorm",
     "fdl_block_attn_workspace_bytes",
     "fdl_block_attn_auto_splits",

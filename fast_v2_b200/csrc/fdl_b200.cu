@@ -267,6 +267,53 @@ int fdl_kv_sparse_prefix(const void* k, const void* v, const int32_t* len, int b
                             kv_sb, kv_ss, kv_sh, out_sb, out_ss, out_sh, stream);
 }
 
+}  // extern "C"
+
+namespace {
+// Score scratch of fdl_kv_sparse_prefix_noalloc: a fixed array in device
+// memory, one per device, alive until the process exits.  Host code must not
+// pass `g_noalloc_scores` itself to a kernel (on the host it names a shadow
+// variable, not device memory); it uses the address looked up per device.
+static __device__ __align__(256) float g_noalloc_scores[FDL_NOALLOC_SCORE_MAX];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[256] = {};
+
+// Device address of g_noalloc_scores on the current device (looked up once
+// per device, with that device current).
+int noalloc_scores_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  if (dev < 0 || dev >= 256) return FDL_E_NODEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scores);
+    if (e != cudaSuccess || !p) return e != cudaSuccess ? -static_cast<int>(e) : FDL_E_NODEVICE;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return FDL_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int fdl_kv_sparse_prefix_noalloc(const void* k, const void* v, const int32_t* len, int batch, int cap, int heads,
+                                 int head_dim, int64_t kv_sb, int64_t kv_ss, int64_t kv_sh, int keep_num,
+                                 int keep_den, int max_keep, int32_t* sel, int32_t* out_len, void* k_out,
+                                 void* v_out, int64_t out_sb, int64_t out_ss, int64_t out_sh, fdl_stream_t stream) {
+  if (batch < 1 || cap < 1) return FDL_E_SHAPE;
+  if (static_cast<int64_t>(batch) * cap > FDL_NOALLOC_SCORE_MAX) return FDL_E_WORKSPACE;
+  void* scores = nullptr;
+  const int rc = noalloc_scores_address(&scores);
+  if (rc != FDL_OK) return rc;
+  return fdl_kv_sparse_prefix(k, v, len, batch, cap, heads, head_dim, kv_sb, kv_ss, kv_sh, keep_num, keep_den,
+                              max_keep, sel, out_len, k_out, v_out, out_sb, out_ss, out_sh, scores,
+                              static_cast<int64_t>(FDL_NOALLOC_SCORE_MAX) * sizeof(float), stream);
+}
+
 int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb, const void* w, float eps, void* gathered,
                        void* normed, int batch, int seq, int n_tok, int hidden, int x_dtype, int64_t x_sb,
                        int64_t x_ss, int64_t out_sb, int64_t out_ss, fdl_stream_t stream) {

@@ -176,6 +176,34 @@ int fdl_kv_sparse_prefix(const void* k, const void* v, const int32_t* len,
                          fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * fdl_kv_sparse_prefix without a workspace argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory --
+ * code running inside another framework's memory pool, hosts that forbid
+ * cudaMalloc after start-up, or bindings that only pass the tensors they
+ * already own.  Same arguments and results as fdl_kv_sparse_prefix; the
+ * per-token score scratch lives in a fixed device array of
+ * FDL_NOALLOC_SCORE_MAX floats (4 MiB) inside the library, held by every GPU
+ * that loads the library until the process exits.
+ *   - batch * cap must not exceed FDL_NOALLOC_SCORE_MAX, else FDL_E_WORKSPACE
+ *     is returned and nothing is launched;
+ *   - the first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture;
+ *   - all calls share the one array: calls that may overlap on the GPU (other
+ *     streams, other threads on the same device) race and must be serialised
+ *     by the caller.  Nothing in the array needs to start at zero.
+ * Allocates nothing (no cudaMalloc / cudaFree, no library allocator).
+ * ---------------------------------------------------------------------- */
+#define FDL_NOALLOC_SCORE_MAX (1 << 20)
+int fdl_kv_sparse_prefix_noalloc(const void* k, const void* v, const int32_t* len,
+                                 int batch, int cap, int heads, int head_dim,
+                                 int64_t kv_sb, int64_t kv_ss, int64_t kv_sh,
+                                 int keep_num, int keep_den, int max_keep,
+                                 int32_t* sel, int32_t* out_len,
+                                 void* k_out, void* v_out,
+                                 int64_t out_sb, int64_t out_ss, int64_t out_sh,
+                                 fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * (c) Fused gather + RMSNorm.
  *
  * For b < B, t < T:  row = x[b, idx[b, t], :]  (length H)
