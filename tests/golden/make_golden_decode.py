@@ -183,12 +183,59 @@ def run(dtype, record=False):
     return prompt, out, trace
 
 
+def replay_trace(dtype, trace):
+    """Teacher-forced replay of a recorded sampler trace through the reference
+    model in `dtype`: the same forwards in the same order, with the cache
+    objects the sampler would hold (DynamicCache across blocks, a fresh
+    DynamicBlockKV per block).  Returns (argmax, top logit) per record."""
+    from transformers.cache_utils import DynamicCache
+
+    modeling, gf, cfg_cls = load_reference()
+    from utils.dynamic_block_kv import DynamicBlockKV
+
+    model = build_reference_model(modeling, cfg_cls, dtype)
+    pkv, block_kv, res = None, None, []
+    with torch.no_grad():
+        for t in trace:
+            if t["kind"] == 0:
+                out = model.forward(input_ids=t["ids"], use_cache=True, past_key_values=pkv,
+                                    update_past_key_values=True, block_size=32)
+                pkv, block_kv = out.past_key_values, None
+            else:
+                if pkv is None:
+                    pkv = DynamicCache()
+                if block_kv is None:
+                    block_kv = DynamicBlockKV(0, GEO["layers"], B, GEO["kv_heads"], 32, GEO["head_dim"], dtype,
+                                              torch.device("cpu"))
+                out = model.forward_dkv(input_ids=t["ids"], use_cache=True, past_key_values=pkv,
+                                        dkv_store=block_kv, fed_indices=t["fed"], is_full_step=t["kind"] == 1)
+            lg = out.logits
+            res.append((torch.softmax(lg, dim=-1).argmax(-1).numpy(), lg.float().max(-1).values.numpy()))
+    return res
+
+
+def gated_agreement(trace, replay, ulps=2.0):
+    """Fraction of positions whose argmax equals the trace's, over positions
+    whose top-2 logit gap exceeds `ulps` bf16 ulps of the top logit."""
+    ok = n = ok_all = n_all = 0
+    for t, (am, top) in zip(trace, replay):
+        ref, gap = t["argmax"].numpy(), t["gap"].numpy()
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(top), 1e-30))) - 7)
+        gate = gap > ulps * ulp
+        ok += int(((am == ref) & gate).sum())
+        n += int(gate.sum())
+        ok_all += int((am == ref).sum())
+        n_all += am.size
+    return ok / max(1, n), ok_all / max(1, n_all)
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     os.environ.setdefault("FAST_DLLM_DKV_REFRESH_STEPS", "4")
     prompt, out_bf16, trace = run(torch.bfloat16, record=True)
     _, out_f32, _ = run(torch.float32)
     agree = (out_bf16[:, PROMPT:] == out_f32[:, PROMPT:]).float().mean().item()
+    tf_gated, tf_all = gated_agreement(trace, replay_trace(torch.float32, trace))
     rec = {}
     for i, t in enumerate(trace):
         rec[f"t{i}_kind"] = np.int64(t["kind"])
@@ -203,10 +250,12 @@ def main():
                         geo=np.array([GEO[k] for k in ("layers", "hidden", "heads", "kv_heads", "head_dim", "ffn",
                                                        "vocab")]),
                         ids_special=np.array([MASK_ID, STOP_ID, PAD_ID]), refresh=np.int64(4),
-                        n_trace=np.int64(len(trace)), ref_bf16_vs_f32_gen_agreement=np.float64(agree), **rec)
+                        n_trace=np.int64(len(trace)), ref_bf16_vs_f32_gen_agreement=np.float64(agree),
+                        ref_tf_f32_agree_gated=np.float64(tf_gated), ref_tf_f32_agree_all=np.float64(tf_all), **rec)
     kinds = [t["kind"] for t in trace]
     print("tokens", tuple(out_bf16.shape), "trace", len(trace), "kinds", {k: kinds.count(k) for k in set(kinds)},
-          "generated-token agreement bf16 vs fp32 reference", f"{agree:.4f}")
+          "generated-token agreement bf16 vs fp32 reference", f"{agree:.4f}",
+          f"teacher-forced fp32-vs-bf16 reference argmax agreement: gated {tf_gated:.4f} all {tf_all:.4f}")
 
 
 if __name__ == "__main__":

@@ -4,8 +4,10 @@ generation_functions.py:2132-2340 on CPU in bf16).
 
 * Teacher-forced parity: every forward the reference sampler ran (prefill,
   full dKV steps, cached dKV steps with their fed indices, commits) is
-  replayed with the same input tokens; the argmax of our logits must equal
-  the reference's at every position whose top-2 logit gap is not a near tie.
+  replayed with the same input tokens; outside near ties, our argmax must
+  agree with the reference's bf16 argmax at least as often (within 0.5 %) as
+  the reference's own fp32 path does -- a bug in positions, masks, fed
+  indices or cache state drops agreement to chance.
 * Free-running greedy agreement is reported, not gated: the tiny random model
   is chaotic -- the reference's own bf16 and fp32 runs agree on only part of
   the generated tokens (stored in the fixture as the noise floor).
@@ -78,9 +80,13 @@ def test_teacher_forced_logits_argmax_match_reference():
                 worst.append((i, kind, int(b), int(t), float(gap[b, t])))
     assert _lib.last_device_error()[0] == 0
     frac = n_ok / max(1, n_gated)
+    # Noise floor: the reference's own fp32 path replayed on the same trace
+    # agrees with its bf16 path this often (make_golden_decode.py).
+    floor = float(g["ref_tf_f32_agree_gated"])
     print(f"teacher-forced argmax agreement: {n_ok}/{n_gated} gated ({frac:.4f}), "
-          f"{n_all_ok}/{n_all} all positions ({n_all_ok / n_all:.4f})")
-    assert frac >= 0.99, f"argmax mismatches outside near ties (trace, kind, b, pos, gap): {worst[:10]}"
+          f"{n_all_ok}/{n_all} all positions ({n_all_ok / n_all:.4f}); reference fp32-vs-bf16 floor "
+          f"{floor:.4f} gated, {float(g['ref_tf_f32_agree_all']):.4f} all")
+    assert frac >= floor - 0.005, f"argmax mismatches outside near ties (trace, kind, b, pos, gap): {worst[:10]}"
 
 
 def test_free_running_greedy_agreement_reported():
