@@ -1,29 +1,38 @@
 // (d) Block attention over the KV cache on sm_100a: TMA -> shared memory,
-// tcgen05.mma (bf16 in, fp32 accumulate in TMEM), online softmax in
-// registers, GQA packed into the MMA M dimension.
+// tcgen05.mma (bf16 in, fp32 accumulate in TMEM), online softmax,
+// GQA packed into the MMA M dimension.
 //
 // One CTA = (batch row b, KV head g, query chunk, KV split).  The G = Hq/Hkv
 // query heads that share KV head g, times the qc queries of the chunk, form
 // R = G*qc <= 256 rows (224 for the 7B geometry: 7 heads x 32 queries),
 // processed as one or two 128-row MMA tiles against the same K/V tiles -- the
-// GQA expansion never touches memory.  Keys stream in tiles of 64 through a
-// 3-stage TMA pipeline.
+// GQA expansion never touches memory.  Keys stream in tiles of 128 through a
+// 2-stage TMA pipeline (64 KB of K+V per stage).
 //
 // Warp roles (320 threads):
 //   warp 0      TMA producer (Q once, then K/V tiles)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2..5  softmax for rows   0..127 (TMEM lanes = rows)
 //   warps 6..9  softmax for rows 128..255
-// Per tile j and row tile m:  S_m = Q_m K_j^T  (TMEM, 64 fp32 columns)  ->
-// softmax warps load S, mask, update the running max (O in TMEM is rescaled
-// only when the max grows by more than 2^8, otherwise the stale max is kept:
-// the result is identical up to rounding), write P = exp2(S - max) as bf16
-// into a 128B-swizzled shared tile  ->  O_m += P V_j  (TMEM, 128 columns).
-// S_m(j+1) is issued as soon as S_m(j) has been read, so the tensor core
-// overlaps the softmax of the current tile.
+// Per key tile j and row tile m:
+//   S_m = Q_m K_j^T          tcgen05.mma, A and B from shared memory,
+//                            128 fp32 TMEM columns
+//   softmax warps            two passes over S_m in 32-column chunks: row max,
+//                            then P = exp2(S - max) written back as bf16 into
+//                            the first 64 columns of S_m's own TMEM range;
+//                            O_m is rescaled in TMEM only when the row max
+//                            grows by more than 2^8 (the stale max is kept
+//                            otherwise -- identical up to rounding)
+//   O_m += P_m V_j           tcgen05.mma with A read from TMEM, B (V,
+//                            head-dim contiguous) from shared memory
+// S_m(j+1) overwrites the TMEM that P_m(j) * V_j reads, and tcgen05.mma
+// orders only MMAs that share an accumulator, so the issuer waits for the
+// completion of P_m(j) * V_j before issuing S_m(j+1); the two row tiles
+// alternate (ping-pong) so the tensor core has the other tile's work queued
+// during that wait and the softmax of one tile overlaps the MMAs of the other.
 //
-// TMEM columns: S_0 [0,64) S_1 [64,128) O_0 [128,256) O_1 [256,384).
-// Shared memory: Q 64 KB | K 3x16 KB | V 3x16 KB | P 2x16 KB | barriers.
+// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
+// Shared memory: Q 64 KB | K 2x32 KB | V 2x32 KB | barriers.
 #pragma once
 #include <cuda.h>
 #include "sm100_ptx.cuh"
@@ -31,24 +40,22 @@
 namespace fdl {
 
 constexpr int kAttnThreads = 320;
-constexpr int kBlockN = 64;
-constexpr int kStages = 3;
+constexpr int kBlockN = 128;
+constexpr int kStages = 2;
 constexpr int kHeadDim = 128;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;
-constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kTmemS = 0;    // + m * 128
+constexpr uint32_t kTmemO = 256;  // + m * 128
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 
 constexpr uint32_t kSmemQ = 0;                        // 2 halves x 256 rows x 128 B
 constexpr uint32_t kQHalf = 256 * 128;                // 32 KB
 constexpr uint32_t kSmemK = 2 * kQHalf;               // 65536
-constexpr uint32_t kKVHalf = kBlockN * 128;           // 8 KB (64 keys x 64 dims)
-constexpr uint32_t kKVTile = 2 * kKVHalf;             // 16 KB
+constexpr uint32_t kKVHalf = kBlockN * 128;           // 16 KB (128 keys x 64 dims)
+constexpr uint32_t kKVTile = 2 * kKVHalf;             // 32 KB
 constexpr uint32_t kSmemV = kSmemK + kStages * kKVTile;
-constexpr uint32_t kSmemP = kSmemV + kStages * kKVTile;
-constexpr uint32_t kPTile = 128 * 128;                // 128 rows x 64 keys bf16
-constexpr uint32_t kSmemBar = kSmemP + 2 * kPTile;    // 196608
-constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignment slack
+constexpr uint32_t kSmemBar = kSmemV + kStages * kKVTile;  // 196608
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;     // + barriers + alignment slack
 
 struct AttnParams {
   CUtensorMap tm_q;   // dims (D, Hq, Sq, B), box (64, G, qc, 1)
@@ -71,10 +78,9 @@ struct AttnBarriers {
   uint64_t q_full;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
+  uint64_t s_full[2];   // S_m(j) complete (and with it P_m(j-1) * V_(j-1))
+  uint64_t p_full[2];   // P_m(j) written to TMEM (4 warp arrivals)
+  uint64_t pv_done[2];  // P_m(j) * V_j complete
   uint64_t fin;
   uint32_t tmem_base;
   int abort;
@@ -147,7 +153,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     }
     for (int m = 0; m < 2; ++m) {
       ptx::mbar_init(&bars->s_full[m], 1);
-      ptx::mbar_init(&bars->s_empty[m], 4);
       ptx::mbar_init(&bars->p_full[m], 4);
       ptx::mbar_init(&bars->pv_done[m], 1);
     }
@@ -221,9 +226,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       const uint32_t q_base = ptx::smem_u32(smem + kSmemQ);
       const uint32_t k_base = ptx::smem_u32(smem + kSmemK);
       const uint32_t v_base = ptx::smem_u32(smem + kSmemV);
-      const uint32_t p_base = ptx::smem_u32(smem + kSmemP);
       bool issued_any = false;
-      // S_m(st) = Q_m * K_st^T : 8 MMAs of K = 16 over the 128 head dims.
+      // S_m = Q_m * K_st^T: 8 MMAs of K = 16 over the 128 head dims.
       auto issue_s = [&](int m, int st) {
         const uint32_t d = tmem + kTmemS + m * kBlockN;
 #pragma unroll
@@ -234,16 +238,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           ptx::mma_bf16_ss(d, a, bd, idesc_s, kk > 0);
         }
       };
-      // O_m += P_m * V_st : 4 MMAs of K = 16 over the 64 keys; V is MN-major
-      // (head dim contiguous): LBO = distance between the two 64-dim halves,
+      // O_m += P_m * V_st: 8 MMAs of K = 16 over the 128 keys.  P_m is read
+      // from TMEM (8 packed columns per 16 keys); V is MN-major (head dim
+      // contiguous): LBO = distance between the two 64-dim halves,
       // SBO = 8 keys x 128 B.
       auto issue_pv = [&](int m, int st, bool acc) {
         const uint32_t d = tmem + kTmemO + m * kHeadDim;
+        const uint32_t a = tmem + kTmemS + m * kBlockN;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a = ptx::smem_desc_sw128(p_base + m * kPTile + kk * 32, 16, 1024);
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
           const uint64_t bd = ptx::smem_desc_sw128(v_base + st * kKVTile + kk * 16 * 128, kKVHalf, 1024);
-          ptx::mma_bf16_ss(d, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+          ptx::mma_bf16_ts(d, a + kk * 8, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = ptx::mbar_wait(&bars->q_full, 0, abort, kWaitTimeoutNs, 2) &&
@@ -259,27 +264,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       for (int j = 0; ok && j < T; ++j) {
         const int st = j % kStages;
         const bool nxt = j + 1 < T;
-        if (nxt) {
-          ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort, kWaitTimeoutNs, 4);
-          if (!ok) break;
-        }
         for (int m = 0; ok && m < p.n_mt; ++m) {
-          if (nxt) {
-            ok = ptx::mbar_wait(&bars->s_empty[m], j & 1, abort, kWaitTimeoutNs, 5);
-            if (!ok) break;
-            ptx::tc_fence_after();
-            issue_s(m, (j + 1) % kStages);
-            ptx::mma_commit(&bars->s_full[m]);
-          }
           ok = ptx::mbar_wait(&bars->p_full[m], j & 1, abort, kWaitTimeoutNs, 6);
           if (!ok) break;
           ptx::tc_fence_after();
           issue_pv(m, st, j > 0);
           ptx::mma_commit(&bars->pv_done[m]);
+          if (nxt) {
+            if (m == 0) {
+              ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort,
+                                  kWaitTimeoutNs, 4);
+              if (!ok) break;
+            }
+            // S_m(j+1) overwrites P_m(j): wait until P_m(j) * V_j has completed.
+            ok = ptx::mbar_wait(&bars->pv_done[m], j & 1, abort, kWaitTimeoutNs, 5);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            issue_s(m, (j + 1) % kStages);
+            ptx::mma_commit(&bars->s_full[m]);
+          }
         }
         // Only stages the producer will refill get a release; no asynchronous
         // arrive may still be pending when the CTA exits.
-        if (j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
+        if (ok && j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
       }
       if (issued_any && !ok) {
         ptx::mma_commit(&bars->fin);
@@ -306,38 +313,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tmem + lane_off + kTmemS + m * kBlockN;
     const uint32_t t_o = tmem + lane_off + kTmemO + m * kHeadDim;
-    uint8_t* prow = smem + kSmemP + m * kPTile + (row >> 3) * 1024 + (row & 7) * 128;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < T; ++j) {
+      // S_m(j) ready (and P_m(j-1) * V_(j-1) done: O_m is stable).
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], j & 1, abort, kWaitTimeoutNs, 7));
       if (!ok) break;
       ptx::tc_fence_after();
-      float s[64];
-      ptx::tmem_ld32(t_s, *reinterpret_cast<float(*)[32]>(&s[0]));
-      ptx::tmem_ld32(t_s + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
-      ptx::tmem_wait_ld();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars->s_empty[m]);
-
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
-      // Visible keys of this tile for this row form a prefix of the tile, so
-      // the mask is one compare per element (no division in the loop).
+      // Visible keys of this tile for this row form a prefix of the tile.
       const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : 0;
+      // Pass 1: row max over the visible keys.
       float tmax = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kBlockN / 32; ++c) {
+        float sv[32];
+        ptx::tmem_ld32(t_s + c * 32, sv);
+        ptx::tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = c < climit ? s[c] * p.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, s[c]);
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < climit) tmax = fmaxf(tmax, sv[i]);
       }
+      tmax *= p.scale_log2;  // scale > 0: max commutes with the scaling
       const float m_new = fmaxf(m_used, tmax);
       const bool grow = m_new > m_used + 8.f;  // true on the first finite max
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[m], (j - 1) & 1, abort, kWaitTimeoutNs, 8));
-        if (!ok) break;
-        ptx::tc_fence_after();
-      }
       const bool rescale = grow && (m_used != -INFINITY) && j > 0;
       if (__any_sync(0xffffffffu, rescale)) {
         const float alpha = rescale ? ptx::ex2(m_used - m_new) : 1.f;
@@ -350,29 +349,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
           ptx::tmem_st32(t_o + ch * 32, o);
         }
-        ptx::tmem_wait_st();
       }
       if (grow) {
         l = (m_used == -INFINITY) ? 0.f : l * ptx::ex2(m_used - m_new);
         m_used = m_new;
       }
+      // Pass 2: P = exp2(S * scale - max) as bf16, packed two per column into
+      // columns [16c, 16c + 16) -- always columns of chunks already read.
       float rsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kBlockN / 32; ++c) {
+        float sv[32];
+        ptx::tmem_ld32(t_s + c * 32, sv);
+        ptx::tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x0 = s[c8 * 8 + 2 * e], x1 = s[c8 * 8 + 2 * e + 1];
-          const float p0 = (x0 == -INFINITY) ? 0.f : ptx::ex2(x0 - m_used);
-          const float p1 = (x1 == -INFINITY) ? 0.f : ptx::ex2(x1 - m_used);
+        for (int i = 0; i < 16; ++i) {
+          const int k0 = c * 32 + 2 * i;
+          const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, -m_used)) : 0.f;
+          const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, -m_used)) : 0.f;
+          rsum += p0 + p1;
           const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-          rsum += __low2float(h) + __high2float(h);
-          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        ptx::tmem_st16(t_s + c * 16, pk);
       }
       l += rsum;
-      ptx::fence_proxy_async_smem();
+      ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars->p_full[m]);
