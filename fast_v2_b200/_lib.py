@@ -29,6 +29,8 @@ EXPORTS = (
     "fdl_block_attn_workspace_bytes",
     "fdl_block_attn_auto_splits",
     "fdl_block_attn",
+    "fdl_rope_qkv",
+    "fdl_swiglu",
     "fdl_last_device_error",
     "fdl_version",
 )

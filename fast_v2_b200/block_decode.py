@@ -111,7 +111,7 @@ class BlockDiffusionLM:
         self.norm = torch.ones(g.hidden, dtype=dtype, device=self.device)
         self.lm_head = self.embed if g.tie_embeddings else normal(g.vocab, g.hidden)
         inv = 1.0 / (g.rope_theta ** (torch.arange(0, g.head_dim, 2, dtype=torch.int64).float() / g.head_dim))
-        self.inv_freq = inv.to(self.device)
+        self.inv_freq = inv.to(self.device).contiguous()
 
     # ------------------------------------------------------------------ ops
     def rmsnorm(self, x, w):
@@ -120,36 +120,29 @@ class BlockDiffusionLM:
         _lib.count_launches(1)
         return out
 
-    def rope(self, pos):
-        """cos/sin [B, T, D] for integer positions [B, T] (Fast_dLLM_QwenRotaryEmbedding,
-        modeling.py:545-560: fp32 angles, cast to the model dtype)."""
-        f = pos.float()[..., None] * self.inv_freq[None, None, :]
-        emb = torch.cat((f, f), dim=-1)
-        return emb.cos().to(self.dtype), emb.sin().to(self.dtype)
-
-    @staticmethod
-    def apply_rope(x, cos, sin):
-        """x * cos + rotate_half(x) * sin on BSHD (modeling.py:186-199)."""
-        cos, sin = cos.unsqueeze(2), sin.unsqueeze(2)
-        h = x.shape[-1] // 2
-        return x * cos + torch.cat((-x[..., h:], x[..., :h]), dim=-1) * sin
-
-    def qkv(self, layer, x, cos, sin):
+    def qkv(self, layer, x, pos):
+        """Fused q/k/v projection (cuBLAS, bias in the epilogue), then one fdl
+        kernel that splits it and applies the rotary embedding at integer
+        positions pos [B, T]."""
         g = self.geo
         B, T, _ = x.shape
-        y = torch.addmm(layer["bqkv"], x.view(B * T, -1), layer["wqkv"].t()).view(B, T, -1)
-        q = y[..., : g.heads * g.head_dim].view(B, T, g.heads, g.head_dim)
-        k = y[..., g.heads * g.head_dim: (g.heads + g.kv_heads) * g.head_dim].view(B, T, g.kv_heads, g.head_dim)
-        v = y[..., (g.heads + g.kv_heads) * g.head_dim:].view(B, T, g.kv_heads, g.head_dim)
-        return self.apply_rope(q, cos, sin).contiguous(), self.apply_rope(k, cos, sin).contiguous(), v.contiguous()
+        y = torch.addmm(layer["bqkv"], x.view(B * T, -1), layer["wqkv"].t())
+        q = torch.empty(B, T, g.heads, g.head_dim, dtype=self.dtype, device=self.device)
+        k = torch.empty(B, T, g.kv_heads, g.head_dim, dtype=self.dtype, device=self.device)
+        v = torch.empty_like(k)
+        torch.ops.fdl.rope_qkv(y, pos.reshape(-1), self.inv_freq, g.heads, g.kv_heads, q, k, v)
+        _lib.count_launches(1)
+        return q, k, v
 
     def mlp_residual(self, layer, h):
         g = self.geo
         B, T, _ = h.shape
         x = self.rmsnorm(h, layer["ln2"])
-        gu = (x.view(B * T, -1) @ layer["wgu"].t()).view(B, T, 2 * g.ffn)
-        act = F.silu(gu[..., : g.ffn]) * gu[..., g.ffn:]
-        return h + (act.view(B * T, -1) @ layer["wd"].t()).view(B, T, -1)
+        gu = x.view(B * T, -1) @ layer["wgu"].t()
+        act = torch.empty(B * T, g.ffn, dtype=self.dtype, device=self.device)
+        torch.ops.fdl.swiglu(gu, act)
+        _lib.count_launches(1)
+        return h + (act @ layer["wd"].t()).view(B, T, -1)
 
     def logits_rows(self, h_final_normed_rows):
         return h_final_normed_rows @ self.lm_head.t()
@@ -227,11 +220,11 @@ class DecodeState:
         m = self.model
         B, T = ids.shape
         h = F.embedding(ids, m.embed)
-        cos, sin = m.rope(pos)
+        pos = pos.contiguous()
         qpos = pos.to(torch.int32).contiguous()
         for l, layer in enumerate(m.layers):
             x = m.rmsnorm(h, layer["ln1"])
-            q, k, v = m.qkv(layer, x, cos, sin)
+            q, k, v = m.qkv(layer, x, pos)
             a = self.attend(q, l, "full", k, v, qpos)
             torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
             _lib.count_launches(1)
@@ -258,11 +251,11 @@ class DecodeState:
             h = F.embedding(torch.gather(ids, 1, fed), m.embed)
             p = torch.gather(pos, 1, fed)
         T = h.shape[1]
-        cos, sin = m.rope(p)
+        p = p.contiguous()
         qpos = p.to(torch.int32).contiguous()
         for l, layer in enumerate(m.layers):
             x = m.rmsnorm(h, layer["ln1"])
-            q, k, v = m.qkv(layer, x, cos, sin)
+            q, k, v = m.qkv(layer, x, p)
             bk, bv = self.blk_k[l], self.blk_v[l]
             if fed is None:
                 torch.ops.fdl.kv_append([bk.transpose(1, 2)], [bv.transpose(1, 2)], [k], [v], self.zero)

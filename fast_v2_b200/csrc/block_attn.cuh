@@ -17,9 +17,10 @@
 // Per key tile j and row tile m:
 //   S_m = Q_m K_j^T          tcgen05.mma, A and B from shared memory,
 //                            128 fp32 TMEM columns
-//   softmax warps            two passes over S_m in 32-column chunks: row max,
-//                            then P = exp2(S - max) written back as bf16 into
-//                            the first 64 columns of S_m's own TMEM range;
+//   softmax warps            S_m row loaded into registers (one TMEM wait),
+//                            row max, then P = exp2(S - max) written back as
+//                            bf16 into the first 64 columns of S_m's own
+//                            TMEM range;
 //                            O_m is rescaled in TMEM only when the row max
 //                            grows by more than 2^8 (the stale max is kept
 //                            otherwise -- identical up to rounding)
@@ -323,16 +324,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
       // Visible keys of this tile for this row form a prefix of the tile.
       const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : 0;
-      // Pass 1: row max over the visible keys.
+      // The whole S row (128 fp32 columns) is loaded with four back-to-back
+      // TMEM loads and a single wait, then kept in registers.
+      float sv0[32], sv1[32], sv2[32], sv3[32];
+      ptx::tmem_ld32(t_s + 0, sv0);
+      ptx::tmem_ld32(t_s + 32, sv1);
+      ptx::tmem_ld32(t_s + 64, sv2);
+      ptx::tmem_ld32(t_s + 96, sv3);
+      ptx::tmem_wait_ld();
       float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kBlockN / 32; ++c) {
-        float sv[32];
-        ptx::tmem_ld32(t_s + c * 32, sv);
-        ptx::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < climit) tmax = fmaxf(tmax, sv[i]);
+      for (int i = 0; i < 32; ++i) {
+        if (i < climit) tmax = fmaxf(tmax, sv0[i]);
+        if (32 + i < climit) tmax = fmaxf(tmax, sv1[i]);
+        if (64 + i < climit) tmax = fmaxf(tmax, sv2[i]);
+        if (96 + i < climit) tmax = fmaxf(tmax, sv3[i]);
       }
       tmax *= p.scale_log2;  // scale > 0: max commutes with the scaling
       const float m_new = fmaxf(m_used, tmax);
@@ -354,26 +360,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         l = (m_used == -INFINITY) ? 0.f : l * ptx::ex2(m_used - m_new);
         m_used = m_new;
       }
-      // Pass 2: P = exp2(S * scale - max) as bf16, packed two per column into
-      // columns [16c, 16c + 16) -- always columns of chunks already read.
+      // P = exp2(S * scale - max) as bf16, packed two per column into the
+      // first 64 columns of S_m (already read into registers).
       float rsum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kBlockN / 32; ++c) {
-        float sv[32];
-        ptx::tmem_ld32(t_s + c * 32, sv);
-        ptx::tmem_wait_ld();
+      const float neg_m = -m_used;
+      auto emit = [&](const float (&sv)[32], int c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k0 = c * 32 + 2 * i;
-          const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, -m_used)) : 0.f;
-          const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, -m_used)) : 0.f;
+          const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, neg_m)) : 0.f;
+          const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, neg_m)) : 0.f;
           rsum += p0 + p1;
           const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
           pk[i] = *reinterpret_cast<const uint32_t*>(&h);
         }
         ptx::tmem_st16(t_s + c * 16, pk);
-      }
+      };
+      emit(sv0, 0);
+      emit(sv1, 1);
+      emit(sv2, 2);
+      emit(sv3, 3);
       l += rsum;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();

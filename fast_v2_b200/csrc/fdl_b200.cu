@@ -10,6 +10,7 @@
 #include "gather_rmsnorm.cuh"
 #include "sparse_prefix.cuh"
 #include "block_attn.cuh"
+#include "rope_swiglu.cuh"
 
 using namespace fdl;
 
@@ -447,6 +448,33 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
   if (rc != FDL_OK || splits == 1) return rc;
   attn_combine_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(p.ws_o, p.ws_lse, p.out, splits, batch,
                                                                             sq, hq, o_sb, o_ss, o_sh);
+  return launch_status();
+}
+
+int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* inv_freq, void* q, void* k, void* v,
+                 int rows, int hq, int hkv, int head_dim, fdl_stream_t stream) {
+  if (!y || !pos || !inv_freq || !q || !k || !v) return FDL_E_NULL;
+  if (rows < 0 || hq < 1 || hkv < 1 || head_dim < 16 || head_dim % 16 || head_dim / 2 > kRopeMaxHalf)
+    return FDL_E_SHAPE;
+  if (rows == 0) return FDL_OK;
+  if (!aligned16(y) || !aligned16(q) || !aligned16(k) || !aligned16(v) || (y_rs * 2) % 16) return FDL_E_ALIGN;
+  RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
+             static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), rows, hq, hkv, head_dim};
+  rope_qkv_kernel<<<rows, kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int64_t rows, int ffn,
+               fdl_stream_t stream) {
+  if (!gu || !out) return FDL_E_NULL;
+  if (rows < 0 || ffn < 8 || ffn % 8) return FDL_E_SHAPE;
+  if (rows == 0) return FDL_OK;
+  if (!aligned16(gu) || !aligned16(out) || (gu_rs * 2) % 16 || (out_rs * 2) % 16) return FDL_E_ALIGN;
+  SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn};
+  const int64_t vecs = rows * (ffn / 8);
+  const int64_t blocks = (vecs + kSwigluThreads - 1) / kSwigluThreads;
+  const int grid = static_cast<int>(blocks < 148 * 16 ? blocks : 148 * 16);
+  swiglu_kernel<<<grid, kSwigluThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 

@@ -358,6 +358,48 @@ void block_attn(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor&
            "block_attn");
 }
 
+// ---------------------------------------------------------------- decode forward glue
+void rope_qkv(const Tensor& y, const Tensor& pos, const Tensor& inv_freq, int64_t hq, int64_t hkv, const Tensor& q,
+              const Tensor& k, const Tensor& v) {
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.stride(-1) == 1,
+              "fdl.rope_qkv: y must be a bf16 CUDA tensor with unit inner stride");
+  const int64_t D = q.size(-1);
+  const int64_t rows = y.numel() / y.size(-1);
+  TORCH_CHECK(y.size(-1) == (hq + 2 * hkv) * D, "fdl.rope_qkv: y last dim ", y.size(-1), " != (hq+2hkv)*D");
+  TORCH_CHECK(y.dim() == 2 || (y.dim() == 3 && y.stride(0) == y.size(1) * y.stride(1)),
+              "fdl.rope_qkv: y rows must be uniformly strided");
+  TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kLong && pos.is_contiguous() && pos.numel() == rows,
+              "fdl.rope_qkv: pos must be a contiguous CUDA int64 tensor with one entry per row");
+  TORCH_CHECK(inv_freq.is_cuda() && inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == D / 2,
+              "fdl.rope_qkv: inv_freq must be CUDA fp32 [D/2]");
+  for (const Tensor* t : {&q, &k, &v})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                "fdl.rope_qkv: outputs must be contiguous bf16 CUDA tensors");
+  TORCH_CHECK(q.numel() == rows * hq * D && k.numel() == rows * hkv * D && v.numel() == rows * hkv * D,
+              "fdl.rope_qkv: output sizes");
+  c10::cuda::CUDAGuard guard(y.device());
+  check_rc(fdl_rope_qkv(y.data_ptr(), y.stride(-2), pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
+                        q.data_ptr(), k.data_ptr(), v.data_ptr(), static_cast<int>(rows), static_cast<int>(hq),
+                        static_cast<int>(hkv), static_cast<int>(D), cur_stream()),
+           "rope_qkv");
+}
+
+void swiglu(const Tensor& gu, const Tensor& out) {
+  TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.stride(-1) == 1 && out.is_cuda() &&
+                  out.scalar_type() == at::kBFloat16 && out.stride(-1) == 1,
+              "fdl.swiglu: bf16 CUDA tensors with unit inner stride");
+  const int64_t F = out.size(-1);
+  const int64_t rows = out.numel() / F;
+  TORCH_CHECK(gu.size(-1) == 2 * F && gu.numel() / gu.size(-1) == rows, "fdl.swiglu: gu must be [rows, 2F]");
+  TORCH_CHECK((gu.dim() == 2 || gu.stride(0) == gu.size(1) * gu.stride(1)) &&
+                  (out.dim() == 2 || out.stride(0) == out.size(1) * out.stride(1)),
+              "fdl.swiglu: rows must be uniformly strided");
+  c10::cuda::CUDAGuard guard(gu.device());
+  check_rc(fdl_swiglu(gu.data_ptr(), gu.stride(-2), out.data_ptr(), out.stride(-2), rows, static_cast<int>(F),
+                      cur_stream()),
+           "swiglu");
+}
+
 // Functional form with the signature of the flash_kvcache custom op of
 // utils/attention_backends.py:83-86; workspace comes from torch's caching
 // allocator (graph-capture safe).
@@ -400,6 +442,9 @@ TORCH_LIBRARY(fdl, m) {
         "int mask_block, float scale, Tensor(a!) out, Tensor(b!)? workspace, int num_splits) -> ()");
   m.def("flash_kvcache(Tensor q, Tensor k_cache, Tensor v_cache, Tensor cache_seqlens, float softmax_scale, "
         "bool causal) -> Tensor");
+  m.def("rope_qkv(Tensor y, Tensor pos, Tensor inv_freq, int hq, int hkv, Tensor(a!) q, Tensor(b!) k, "
+        "Tensor(c!) v) -> ()");
+  m.def("swiglu(Tensor gu, Tensor(a!) out) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
@@ -411,6 +456,8 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("gather_rmsnorm", &gather_rmsnorm);
   m.impl("block_attn", &block_attn);
   m.impl("flash_kvcache", &flash_kvcache);
+  m.impl("rope_qkv", &rope_qkv);
+  m.impl("swiglu", &swiglu);
 }
 
 TORCH_LIBRARY_IMPL(fdl, Meta, m) {
@@ -431,4 +478,7 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
                           const std::optional<Tensor>&, const std::optional<Tensor>&, int64_t, double, const Tensor&,
                           const std::optional<Tensor>&, int64_t) {});
   m.impl("flash_kvcache", &flash_kvcache_meta);
+  m.impl("rope_qkv", [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
+                        const Tensor&) {});
+  m.impl("swiglu", [](const Tensor&, const Tensor&) {});
 }

@@ -274,6 +274,30 @@ int fdl_block_attn(const void* q, const void* k, const void* v,
                    fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Decode-forward elementwise stages next to the KV path (single HBM pass).
+ *
+ * fdl_rope_qkv: y is the fused q/k/v projection output, bf16
+ * [rows, (hq + 2*hkv) * head_dim] with row stride y_rs (elements); pos is
+ * device int64 [rows] (absolute positions), inv_freq device fp32
+ * [head_dim/2].  Writes q [rows, hq, D], k [rows, hkv, D] (rotary embedding
+ * applied) and v [rows, hkv, D], contiguous bf16.  Per element, exactly the
+ * reference's bf16 arithmetic: c, s = bf16(cos/sin(fp32(pos * inv_freq)));
+ * out = bf16(bf16(x * c) + bf16(rotate_half(x) * s)).  Replaces the q/k/v
+ * view + _apply_rotary_pos_emb of the patched attention forward
+ * (utils/attention_backends.py:777-788, 829-836) / apply_rotary_pos_emb
+ * (modeling.py:186-199) with the rotary table of modeling.py:545-560.
+ *
+ * fdl_swiglu: gu bf16 [rows, 2F] (gate then up, row stride gu_rs) ->
+ * out [rows, F] (row stride out_rs) = bf16(bf16(silu(gate)) * up)
+ * (Fast_dLLM_QwenMLP.forward, modeling.py:163-165).  F % 8 == 0.
+ * ---------------------------------------------------------------------- */
+int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos,
+                 const float* inv_freq, void* q, void* k, void* v,
+                 int rows, int hq, int hkv, int head_dim, fdl_stream_t stream);
+int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs,
+               int64_t rows, int ffn, fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Status.  Copies the calling device's first recorded device-side error
  * code into *code and the offending value into *info (either may be NULL),
  * then clears both.  Synchronises the device.  Returns 0 or -(cudaError_t).

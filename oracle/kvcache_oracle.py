@@ -276,6 +276,48 @@ def eval_block_mask(seqlen: int, block_size: int, cache_len: int):
 
 
 # --------------------------------------------------------------------------
+# decode-forward elementwise stages next to the KV path
+# --------------------------------------------------------------------------
+
+
+def rope_qkv(y_bits, pos, inv_freq, hq: int, hkv: int):
+    """q/k/v split of the fused projection output and rotary embedding:
+    angle = fp32(pos * inv_freq) (Fast_dLLM_QwenRotaryEmbedding,
+    modeling.py:545-560), c, s = bf16(cos/sin(angle)), and per element
+    bf16(bf16(x * c) + bf16(rotate_half(x) * s)) (apply_rotary_pos_emb,
+    modeling.py:186-199).  y_bits bf16 [rows, (hq + 2 hkv) * D] -> bits of
+    q [rows, hq, D], k [rows, hkv, D], v [rows, hkv, D]."""
+    rows = y_bits.shape[0]
+    D = 2 * inv_freq.shape[0]
+    y = bf16_to_f32(y_bits).reshape(rows, hq + 2 * hkv, D)
+    ang = (np.asarray(pos, np.float32)[:, None] * inv_freq.astype(np.float32)[None, :]).astype(np.float32)
+    c = bf16_to_f32(f32_to_bf16(np.cos(ang.astype(np.float64)).astype(np.float32)))
+    s = bf16_to_f32(f32_to_bf16(np.sin(ang.astype(np.float64)).astype(np.float32)))
+    c = np.concatenate([c, c], axis=1)[:, None, :]
+    s = np.concatenate([s, s], axis=1)[:, None, :]
+
+    def rnd(x):
+        return bf16_to_f32(f32_to_bf16(x.astype(np.float32)))
+
+    x = y[:, : hq + hkv]
+    h = D // 2
+    rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+    out = f32_to_bf16((rnd(x * c) + rnd(rot * s)).astype(np.float32))
+    v = f32_to_bf16(y[:, hq + hkv:])
+    return out[:, :hq], out[:, hq:], v
+
+
+def swiglu(gu_bits):
+    """bf16(bf16(silu(gate)) * up) over [rows, 2F] (Fast_dLLM_QwenMLP.forward,
+    modeling.py:163-165: act_fn(gate_proj(x)) * up_proj(x) in bf16)."""
+    F_ = gu_bits.shape[1] // 2
+    g = bf16_to_f32(gu_bits[:, :F_]).astype(np.float64)
+    u = bf16_to_f32(gu_bits[:, F_:])
+    s = bf16_to_f32(f32_to_bf16((g / (1.0 + np.exp(-g))).astype(np.float32)))
+    return f32_to_bf16((s * u).astype(np.float32))
+
+
+# --------------------------------------------------------------------------
 # index selection helpers on the path (a18)
 # --------------------------------------------------------------------------
 

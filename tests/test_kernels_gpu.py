@@ -292,3 +292,43 @@ def test_flash_kvcache_functional_op():
     out = torch.ops.fdl.flash_kvcache(q, k, v, seq, 128 ** -0.5, False)
     ref = O.block_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), [512, 100])
     assert_close("flash_kvcache", out.float().cpu().numpy(), ref, ATOL, RTOL)
+
+
+# ------------------------------------------------------------------ decode-forward glue
+def _ulp_mismatch(got_bits, ref_bits):
+    g = O.bf16_to_f32(got_bits).astype(np.float64)
+    r = O.bf16_to_f32(ref_bits).astype(np.float64)
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(r), 1e-30))) - 7)
+    return np.mean(got_bits != ref_bits), np.max(np.abs(g - r) / ulp)
+
+
+def test_rope_qkv_matches_reference_rounding():
+    rows, hq, hkv, D = 96, 28, 4, 128
+    y = rbf16((rows, (hq + 2 * hkv) * D), 61)
+    pos = torch.randint(0, 8192, (rows,), generator=torch.Generator().manual_seed(3))
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))
+    q = torch.empty(rows, hq, D, dtype=torch.bfloat16, device=DEV)
+    k = torch.empty(rows, hkv, D, dtype=torch.bfloat16, device=DEV)
+    v = torch.empty_like(k)
+    torch.ops.fdl.rope_qkv(y.to(DEV), pos.to(DEV), inv.to(DEV), hq, hkv, q, k, v)
+    eq, ek, ev = O.rope_qkv(bits_of(y), pos.numpy(), inv.numpy(), hq, hkv)
+    assert np.array_equal(bits_of(v), ev)
+    for name, got, ref in (("q", q, eq), ("k", k, ek)):
+        frac, worst = _ulp_mismatch(bits_of(got), ref)
+        # cos/sin of CUDA vs a correctly rounded reference can differ in the
+        # last fp32 bit, which flips a bf16 rounding now and then
+        assert frac < 2e-3 and worst <= 2.0, (name, frac, worst)
+
+
+def test_swiglu_matches_reference_rounding():
+    rows, F_ = 257, 18944
+    gu = rbf16((rows, 2 * F_), 71, 3.0)
+    out = torch.empty(rows, F_, dtype=torch.bfloat16, device=DEV)
+    torch.ops.fdl.swiglu(gu.to(DEV), out)
+    ref = O.swiglu(bits_of(gu))
+    frac, worst = _ulp_mismatch(bits_of(out), ref)
+    assert frac < 2e-3 and worst <= 2.0, (frac, worst)
+    # the torch bf16 path the reference runs (silu then multiply, on the GPU)
+    tg = gu.to(DEV)
+    t = torch.nn.functional.silu(tg[:, :F_]) * tg[:, F_:]
+    assert torch.mean((t != out).float()).item() < 2e-3
