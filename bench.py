@@ -422,7 +422,7 @@ def _e2e(args, rank, world, kt, geo_name):
 
         def step():
             with torch.no_grad():
-                _, state["bridge"] = dec.decode_block(state["bridge"], stats=stats)
+                state["blk"], state["bridge"] = dec.decode_block(state["bridge"], stats=stats)
 
         # e2e: the host-facing call per block -- bridge token in from pinned host
         # memory, the block's 32 tokens back to pinned host memory.
@@ -433,8 +433,8 @@ def _e2e(args, rank, world, kt, geo_name):
             with torch.no_grad():
                 hb.copy_(state["bridge"], non_blocking=True)
                 bridge = hb.to("cuda", non_blocking=True)
-                blk, state["bridge"] = dec.decode_block(bridge, stats=stats)
-                hblk.copy_(blk, non_blocking=True)
+                state["blk"], state["bridge"] = dec.decode_block(bridge, stats=stats)
+                hblk.copy_(state["blk"], non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
         # dominant kernel of ours in the step: the block attention of a full
@@ -493,6 +493,7 @@ def _e2e(args, rank, world, kt, geo_name):
         return dict(meta, cpu_sample=cpu_sample)
     kvb, fl = dom_work()
     return dict(meta, units_per_step=B * 32, step=step, dominant=dominant, graph=False, e2e_step=e2e_step,
+                collect=lambda: state["blk"],
                 e2e_bytes=(B * 8, B * 32 * 8),
                 roofline=dict(bound="hbm", per_launch=kvb, kernel="block_attn_kernel (full dKV step, layer 0)",
                               flops=fl, dynamic=dom_work),
@@ -691,6 +692,15 @@ def main():
         e2e = {"value": w["units_per_step"] * n_e2e * world / (ms2 / 1e3), "unit": w["unit"],
                "h2d_bytes_per_step": w["e2e_bytes"][0], "d2h_bytes_per_step": w["e2e_bytes"][1]}
 
+    # Sequence-sharded output: one all-gather of every rank's last generated
+    # block after the timed regions (the only collective besides the max-time
+    # reduction).
+    collected = None
+    if world > 1 and w.get("collect"):
+        from fast_v2_b200.sharding import gather_generated
+
+        collected = list(gather_generated(w["collect"](), pad_id=-1).shape)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
@@ -702,7 +712,8 @@ def main():
             "metric": w["metric"], "value": value, "unit": w["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-            "config": {**w["config"], "parallelism": f"dp{world} (sequence-sharded replicas)"},
+            "config": {**w["config"], "parallelism": f"dp{world} (sequence-sharded replicas)",
+                       **({"gathered_block": collected} if collected else {})},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": sampler.summary(),
             "gpu_launches": (w["launches_per_step"] * args.steps if w["launches_per_step"] is not None
                              else launches_timed),

@@ -31,6 +31,7 @@ EXPORTS = (
     "fdl_block_attn",
     "fdl_rope_qkv",
     "fdl_swiglu",
+    "fdl_add_rmsnorm",
     "fdl_last_device_error",
     "fdl_version",
 )

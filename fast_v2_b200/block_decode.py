@@ -134,15 +134,41 @@ class BlockDiffusionLM:
         _lib.count_launches(1)
         return q, k, v
 
-    def mlp_residual(self, layer, h):
+    def add_rmsnorm(self, y, h, w):
+        """Residual connection and the following RMSNorm in one kernel:
+        h += y in place (bf16 rounding, the layer's `residual + hidden_states`)
+        and returns RMSNorm(h) with weight w."""
+        out = torch.empty_like(h)
+        torch.ops.fdl.add_rmsnorm(y.view_as(h), h, w, self.geo.eps, h, out)
+        _lib.count_launches(1)
+        return out
+
+    def mlp(self, layer, x):
+        """Fast_dLLM_QwenMLP.forward (modeling.py:163-165) on normed rows x:
+        fused gate/up GEMM, one SwiGLU kernel, down GEMM.  The residual add is
+        left to the caller (fused into the next RMSNorm)."""
         g = self.geo
-        B, T, _ = h.shape
-        x = self.rmsnorm(h, layer["ln2"])
+        B, T, _ = x.shape
         gu = x.view(B * T, -1) @ layer["wgu"].t()
         act = torch.empty(B * T, g.ffn, dtype=self.dtype, device=self.device)
         torch.ops.fdl.swiglu(gu, act)
         _lib.count_launches(1)
-        return h + (act @ layer["wd"].t()).view(B, T, -1)
+        return (act @ layer["wd"].t()).view(B, T, -1)
+
+    def layers_forward(self, h, attend_layer):
+        """The decoder stack on hidden states h [B, T, hidden] (updated in
+        place as the residual stream).  attend_layer(l, layer, x) returns the
+        attention output [B, T, Hq * D] of layer l for normed input x.  Each
+        residual add is fused into the RMSNorm that follows it; returns h
+        after the last layer's MLP residual."""
+        B, T, _ = h.shape
+        y = None
+        for l, layer in enumerate(self.layers):
+            x = self.rmsnorm(h, layer["ln1"]) if y is None else self.add_rmsnorm(y, h, layer["ln1"])
+            a = attend_layer(l, layer, x)
+            x = self.add_rmsnorm(a.reshape(B * T, -1) @ layer["wo"].t(), h, layer["ln2"])
+            y = self.mlp(layer, x)
+        return h + y
 
     def logits_rows(self, h_final_normed_rows):
         return h_final_normed_rows @ self.lm_head.t()
@@ -222,14 +248,15 @@ class DecodeState:
         h = F.embedding(ids, m.embed)
         pos = pos.contiguous()
         qpos = pos.to(torch.int32).contiguous()
-        for l, layer in enumerate(m.layers):
-            x = m.rmsnorm(h, layer["ln1"])
+
+        def attend_layer(l, layer, x):
             q, k, v = m.qkv(layer, x, pos)
             a = self.attend(q, l, "full", k, v, qpos)
             torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
             _lib.count_launches(1)
-            h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
-            h = m.mlp_residual(layer, h)
+            return a
+
+        h = m.layers_forward(h, attend_layer)
         self.lens += T
         if all_rows:
             return m.rmsnorm(h, m.norm)
@@ -253,8 +280,8 @@ class DecodeState:
         T = h.shape[1]
         p = p.contiguous()
         qpos = p.to(torch.int32).contiguous()
-        for l, layer in enumerate(m.layers):
-            x = m.rmsnorm(h, layer["ln1"])
+
+        def attend_layer(l, layer, x):
             q, k, v = m.qkv(layer, x, p)
             bk, bv = self.blk_k[l], self.blk_v[l]
             if fed is None:
@@ -262,9 +289,9 @@ class DecodeState:
             else:
                 torch.ops.fdl.kv_scatter(bk, bv, k.transpose(1, 2), v.transpose(1, 2), fed, 2)
             _lib.count_launches(1)
-            a = self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
-            h = h + (a.view(B * T, -1) @ layer["wo"].t()).view(B, T, -1)
-            h = m.mlp_residual(layer, h)
+            return self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
+
+        h = m.layers_forward(h, attend_layer)
         if fed is None:
             return h
         out = seed_hidden.clone()

@@ -31,6 +31,8 @@
 // completion of P_m(j) * V_j before issuing S_m(j+1); the two row tiles
 // alternate (ping-pong) so the tensor core has the other tile's work queued
 // during that wait and the softmax of one tile overlaps the MMAs of the other.
+// (Two issuers, one per row tile, keep the pipe fuller in isolation but slow
+// the softmax warps, which bound the kernel, by more.)
 //
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
 // Shared memory: Q 64 KB | K 2x32 KB | V 2x32 KB | barriers.
@@ -40,7 +42,8 @@
 
 namespace fdl {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnWarps = 10;
+constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kBlockN = 128;
 constexpr int kStages = 2;
 constexpr int kHeadDim = 128;
@@ -48,6 +51,14 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + m * 128
 constexpr uint32_t kTmemO = 256;  // + m * 128
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
+#ifndef FDL_ATTN_EMU_PAIRS
+#define FDL_ATTN_EMU_PAIRS 0
+#endif
+constexpr int kEmuPairs = FDL_ATTN_EMU_PAIRS;
+#ifndef FDL_ATTN_PREFETCH
+#define FDL_ATTN_PREFETCH 1
+#endif
+constexpr int kPrefetch = FDL_ATTN_PREFETCH;  // key tiles prefetched into L2 ahead of the smem ring  // of every 8 exponential pairs, on the FMA pipe
 
 constexpr uint32_t kSmemQ = 0;                        // 2 halves x 256 rows x 128 B
 constexpr uint32_t kQHalf = 256 * 128;                // 32 KB
@@ -192,17 +203,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * qbytes);
       ptx::tma_load_4d(smem + kSmemQ, &p.tm_q, &bars->q_full, 0, g * p.G, q0, b);
       ptx::tma_load_4d(smem + kSmemQ + kQHalf, &p.tm_q, &bars->q_full, 64, g * p.G, q0, b);
+      // Tile j's coordinates in its source map.
+      auto coords = [&](int j, const CUtensorMap*& tk, const CUtensorMap*& tv, int& c1, int& c2) {
+        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+        tk = ti.src ? &p.tm_kb : &p.tm_k;
+        tv = ti.src ? &p.tm_vb : &p.tm_v;
+        const bool hm = ti.src ? p.blk_hmajor : p.kv_hmajor;
+        c1 = hm ? ti.key0 : g;
+        c2 = hm ? g : ti.key0;
+      };
+      // L2 prefetch runs kPrefetch tiles ahead of the shared-memory loads.
+      auto prefetch = [&](int j) {
+        if (j >= T) return;
+        const CUtensorMap *tk, *tv;
+        int c1, c2;
+        coords(j, tk, tv, c1, c2);
+        ptx::tma_prefetch_l2_4d(tk, 0, c1, c2, b);
+        ptx::tma_prefetch_l2_4d(tk, 64, c1, c2, b);
+        ptx::tma_prefetch_l2_4d(tv, 0, c1, c2, b);
+        ptx::tma_prefetch_l2_4d(tv, 64, c1, c2, b);
+      };
+      for (int j = kStages; j < kStages + kPrefetch; ++j) prefetch(j);
       int issued = 0;
       for (int j = 0; j < T; ++j) {
         const int st = j % kStages;
         if (j >= kStages) {
+          prefetch(j + kPrefetch);
           if (!ptx::mbar_wait(&bars->kv_empty[st], ((j / kStages) - 1) & 1, abort, kWaitTimeoutNs, 1)) break;
         }
-        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
-        const CUtensorMap* tk = ti.src ? &p.tm_kb : &p.tm_k;
-        const CUtensorMap* tv = ti.src ? &p.tm_vb : &p.tm_v;
-        const bool hm = ti.src ? p.blk_hmajor : p.kv_hmajor;
-        const int c1 = hm ? ti.key0 : g, c2 = hm ? g : ti.key0;
+        const CUtensorMap *tk, *tv;
+        int c1, c2;
+        coords(j, tk, tv, c1, c2);
         uint8_t* ks = smem + kSmemK + st * kKVTile;
         uint8_t* vs = smem + kSmemV + st * kKVTile;
         ptx::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kKVTile);
@@ -224,19 +255,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     if (lane == 0 && T > 0) {
       const uint32_t idesc_s = ptx::idesc_bf16_f32(128, kBlockN, false);
       const uint32_t idesc_o = ptx::idesc_bf16_f32(128, kHeadDim, true);
-      const uint32_t q_base = ptx::smem_u32(smem + kSmemQ);
-      const uint32_t k_base = ptx::smem_u32(smem + kSmemK);
-      const uint32_t v_base = ptx::smem_u32(smem + kSmemV);
+      // Base descriptors built once; the (16-byte-unit) address field is
+      // advanced by compile-time offsets in the issue loops.
+      const uint64_t q_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemQ), 16, 1024);
+      const uint64_t k_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemK), 16, 1024);
+      const uint64_t v_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemV), kKVHalf, 1024);
       bool issued_any = false;
       // S_m = Q_m * K_st^T: 8 MMAs of K = 16 over the 128 head dims.
       auto issue_s = [&](int m, int st) {
         const uint32_t d = tmem + kTmemS + m * kBlockN;
+        const uint64_t qa = q_desc + static_cast<uint64_t>(m) * (128 * 128 / 16);
+        const uint64_t kb = k_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk & 3) * 32;  // K=16 slice inside the 128-byte swizzle row
-          const uint64_t a = ptx::smem_desc_sw128(q_base + (kk >> 2) * kQHalf + m * 128 * 128 + off, 16, 1024);
-          const uint64_t bd = ptx::smem_desc_sw128(k_base + st * kKVTile + (kk >> 2) * kKVHalf + off, 16, 1024);
-          ptx::mma_bf16_ss(d, a, bd, idesc_s, kk > 0);
+          // K=16 slice kk: 32 bytes into the 128-byte swizzle row of its half.
+          ptx::mma_bf16_ss(d, qa + ((kk >> 2) * kQHalf + (kk & 3) * 32) / 16,
+                           kb + ((kk >> 2) * kKVHalf + (kk & 3) * 32) / 16, idesc_s, kk > 0);
         }
       };
       // O_m += P_m * V_st: 8 MMAs of K = 16 over the 128 keys.  P_m is read
@@ -246,11 +280,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       auto issue_pv = [&](int m, int st, bool acc) {
         const uint32_t d = tmem + kTmemO + m * kHeadDim;
         const uint32_t a = tmem + kTmemS + m * kBlockN;
+        const uint64_t vb = v_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint64_t bd = ptx::smem_desc_sw128(v_base + st * kKVTile + kk * 16 * 128, kKVHalf, 1024);
-          ptx::mma_bf16_ts(d, a + kk * 8, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          ptx::mma_bf16_ts(d, a + kk * 8, vb + (kk * 16 * 128) / 16, idesc_o, (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = ptx::mbar_wait(&bars->q_full, 0, abort, kWaitTimeoutNs, 2) &&
                 ptx::mbar_wait(&bars->kv_full[0], 0, abort, kWaitTimeoutNs, 3);
@@ -271,6 +304,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           ptx::tc_fence_after();
           issue_pv(m, st, j > 0);
           ptx::mma_commit(&bars->pv_done[m]);
+          // Stage st is free once the last row tile's P * V_j completes (only
+          // stages the producer will refill get a release; no asynchronous
+          // arrive may still be pending when the CTA exits).
+          if (m == p.n_mt - 1 && j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
           if (nxt) {
             if (m == 0) {
               ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort,
@@ -285,16 +322,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
             ptx::mma_commit(&bars->s_full[m]);
           }
         }
-        // Only stages the producer will refill get a release; no asynchronous
-        // arrive may still be pending when the CTA exits.
-        if (ok && j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
       }
       if (issued_any && !ok) {
         ptx::mma_commit(&bars->fin);
         drain_wait(&bars->fin, 0);
       }
     }
-  } else if ((warp - 2) / 4 < p.n_mt) {
+  } else if (warp >= 2 && (warp - 2) / 4 < p.n_mt) {
     // ------------------------------------------------------- softmax
     const int m = (warp - 2) >> 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -332,13 +366,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       ptx::tmem_ld32(t_s + 64, sv2);
       ptx::tmem_ld32(t_s + 96, sv3);
       ptx::tmem_wait_ld();
-      float tmax = -INFINITY;
+      // Tiles with every key visible to every row of the warp (all but the
+      // sequence's last tiles) take the unpredicated path.
+      const bool full = __all_sync(0xffffffffu, climit == kBlockN);
+      float tmax;
+      if (full) {
+        float a0 = sv0[0], a1 = sv1[0], a2 = sv2[0], a3 = sv3[0];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (i < climit) tmax = fmaxf(tmax, sv0[i]);
-        if (32 + i < climit) tmax = fmaxf(tmax, sv1[i]);
-        if (64 + i < climit) tmax = fmaxf(tmax, sv2[i]);
-        if (96 + i < climit) tmax = fmaxf(tmax, sv3[i]);
+        for (int i = 1; i < 31; i += 2) {
+          a0 = ptx::fmax3(a0, sv0[i], sv0[i + 1]);
+          a1 = ptx::fmax3(a1, sv1[i], sv1[i + 1]);
+          a2 = ptx::fmax3(a2, sv2[i], sv2[i + 1]);
+          a3 = ptx::fmax3(a3, sv3[i], sv3[i + 1]);
+        }
+        tmax = ptx::fmax3(ptx::fmax3(a0, a1, sv0[31]), ptx::fmax3(a2, a3, sv1[31]), fmaxf(sv2[31], sv3[31]));
+      } else {
+        tmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < climit) tmax = fmaxf(tmax, sv0[i]);
+          if (32 + i < climit) tmax = fmaxf(tmax, sv1[i]);
+          if (64 + i < climit) tmax = fmaxf(tmax, sv2[i]);
+          if (96 + i < climit) tmax = fmaxf(tmax, sv3[i]);
+        }
       }
       tmax *= p.scale_log2;  // scale > 0: max commutes with the scaling
       const float m_new = fmaxf(m_used, tmax);
@@ -364,23 +414,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       // first 64 columns of S_m (already read into registers).
       float rsum = 0.f;
       const float neg_m = -m_used;
-      auto emit = [&](const float (&sv)[32], int c) {
-        uint32_t pk[16];
+      if (full) {
+        // Packed pairs: x = S * scale - max by one f32x2 FMA; kEmuPairs of
+        // every 8 pairs take 2^x from the FMA-pipe polynomial, the rest from
+        // the special-function unit, so the two units share the exponentials.
+        const uint64_t sc2 = ptx::pack2(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = ptx::pack2(neg_m, neg_m);
+        uint64_t acc2 = ptx::pack2(0.f, 0.f);
+        auto emit_full = [&](const float (&sv)[32], int c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = c * 32 + 2 * i;
-          const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, neg_m)) : 0.f;
-          const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, neg_m)) : 0.f;
-          rsum += p0 + p1;
-          const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-          pk[i] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        ptx::tmem_st16(t_s + c * 16, pk);
-      };
-      emit(sv0, 0);
-      emit(sv1, 1);
-      emit(sv2, 2);
-      emit(sv3, 3);
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
+            uint64_t e2;
+            if ((i & 7) < kEmuPairs) {
+              e2 = ptx::exp2_poly2(x2);
+            } else {
+              float x0, x1;
+              ptx::unpack2(x2, x0, x1);
+              e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
+            }
+            acc2 = ptx::add2(acc2, e2);
+            float p0, p1;
+            ptx::unpack2(e2, p0, p1);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          ptx::tmem_st16(t_s + c * 16, pk);
+        };
+        emit_full(sv0, 0);
+        emit_full(sv1, 1);
+        emit_full(sv2, 2);
+        emit_full(sv3, 3);
+        float s0, s1;
+        ptx::unpack2(acc2, s0, s1);
+        rsum = s0 + s1;
+      } else {
+        auto emit = [&](const float (&sv)[32], int c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = c * 32 + 2 * i;
+            const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, neg_m)) : 0.f;
+            const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, neg_m)) : 0.f;
+            rsum += p0 + p1;
+            const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          ptx::tmem_st16(t_s + c * 16, pk);
+        };
+        emit(sv0, 0);
+        emit(sv1, 1);
+        emit(sv2, 2);
+        emit(sv3, 3);
+      }
       l += rsum;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();

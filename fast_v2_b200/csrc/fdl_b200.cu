@@ -2,6 +2,7 @@
 // include/fdl_kvcache.h).  Single translation unit: all kernels share the
 // per-device status word declared in common.cuh.
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <initializer_list>
 #include <mutex>
 
@@ -61,14 +62,26 @@ bool attn_smem_configured() {
   return true;
 }
 
+// Split-KV count for `work_items` (batch x KV head x query chunk) CTAs of
+// about `tiles_est` key tiles each.  Cost model in key-tile times: waves x
+// (per-CTA fixed cost of about 2 tiles -- Q load, TMEM and barrier setup,
+// pipeline fill, epilogue -- plus the CTA's share of the tiles), plus about one
+// tile for the combine pass when split.  One CTA per SM.
 int pick_splits(int work_items, int tiles_est) {
   const int sms = num_sms();
-  if (work_items >= sms) return 1;
-  int s = (2 * sms + work_items - 1) / work_items;
-  const int cap = tiles_est / 4 > 1 ? tiles_est / 4 : 1;
-  if (s > cap) s = cap;
-  if (s > 64) s = 64;
-  return s < 1 ? 1 : s;
+  const int max_s = std::min(64, std::max(1, tiles_est / 2));
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int s = 1; s <= max_s; ++s) {
+    const int64_t waves = (static_cast<int64_t>(work_items) * s + sms - 1) / sms;
+    const int64_t per = (tiles_est + s - 1) / s;
+    const int64_t cost = waves * (2 + per) + (s > 1 ? 1 : 0);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -351,6 +364,38 @@ int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb, const 
   return launch_status();
 }
 
+int fdl_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs, const void* w, float eps,
+                    void* sum_out, void* normed, int64_t out_rs, int rows, int hidden, int x_dtype,
+                    fdl_stream_t stream) {
+  if (!x || !res || !normed) return FDL_E_NULL;
+  if (rows < 0 || hidden < 1) return FDL_E_SHAPE;
+  if (rows == 0) return FDL_OK;
+  int es;
+  switch (x_dtype) {
+    case FDL_BF16: case FDL_F16: es = 2; break;
+    default: return FDL_E_DTYPE;
+  }
+  NormArgs a{};
+  a.x = static_cast<const char*>(x);
+  a.res = static_cast<const char*>(res);
+  a.res_ss = res_rs * es;
+  a.w = static_cast<const char*>(w);
+  a.gathered = static_cast<char*>(sum_out);
+  a.normed = static_cast<char*>(normed);
+  a.eps = eps;
+  a.B = 1; a.S = rows; a.T = rows; a.H = hidden;
+  a.x_sb = 0; a.x_ss = x_rs * es; a.o_sb = 0; a.o_ss = out_rs * es;
+  const uint64_t ptrs = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(res) |
+                        reinterpret_cast<uintptr_t>(sum_out) | reinterpret_cast<uintptr_t>(normed) |
+                        reinterpret_cast<uintptr_t>(w);
+  const bool vec_ok = pick_vec({static_cast<uint64_t>(hidden) * es, ptrs, static_cast<uint64_t>(a.x_ss),
+                                static_cast<uint64_t>(a.res_ss), static_cast<uint64_t>(a.o_ss)}) == 16;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (x_dtype == FDL_BF16) launch_gather_rmsnorm<__nv_bfloat16>(a, vec_ok, s);
+  else launch_gather_rmsnorm<__half>(a, vec_ok, s);
+  return launch_status();
+}
+
 int64_t fdl_block_attn_workspace_bytes(int batch, int sq, int hq, int head_dim, int num_splits) {
   if (num_splits <= 1) return 0;
   const int64_t rows = static_cast<int64_t>(batch) * sq * hq;
@@ -467,13 +512,11 @@ int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* i
 int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int64_t rows, int ffn,
                fdl_stream_t stream) {
   if (!gu || !out) return FDL_E_NULL;
-  if (rows < 0 || ffn < 8 || ffn % 8) return FDL_E_SHAPE;
+  if (rows < 0 || rows > INT32_MAX || ffn < 8 || ffn % 8) return FDL_E_SHAPE;
   if (rows == 0) return FDL_OK;
   if (!aligned16(gu) || !aligned16(out) || (gu_rs * 2) % 16 || (out_rs * 2) % 16) return FDL_E_ALIGN;
   SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn};
-  const int64_t vecs = rows * (ffn / 8);
-  const int64_t blocks = (vecs + kSwigluThreads - 1) / kSwigluThreads;
-  const int grid = static_cast<int>(blocks < 148 * 16 ? blocks : 148 * 16);
+  const dim3 grid(static_cast<unsigned>(rows), (ffn / 8 + kSwigluChunk - 1) / kSwigluChunk);
   swiglu_kernel<<<grid, kSwigluThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }

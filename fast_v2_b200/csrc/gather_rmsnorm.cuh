@@ -13,6 +13,8 @@ constexpr int kNormThreads = 128;  // 4 rows per CTA
 
 struct NormArgs {
   const char* x;
+  const char* res;   // optional residual: rows become round(x + res) before the norm
+  int64_t res_ss;    // residual row stride (bytes); rows are indexed like the output
   const int64_t* idx;
   int64_t idx_sb;
   const char* w;
@@ -74,6 +76,24 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
     const int vi = lane + 32 * k;
     if (vi < nvec) v[k] = ld_stream16(xr + vi * 16);
   }
+  if (a.res) {
+    // Residual connection (decoder layer `residual + hidden_states`): one
+    // rounding to the storage dtype, then the norm of the rounded sum.
+    const char* rr = a.res + static_cast<int64_t>(row) * a.res_ss;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int vi = lane + 32 * k;
+      if (vi < nvec) {
+        // plain load: the sum may be written back over the residual in place
+        const uint4 rv = *reinterpret_cast<const uint4*>(rr + vi * 16);
+        T* e = reinterpret_cast<T*>(&v[k]);
+        const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j)
+          e[j] = ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(e[j]), ElemOps<T>::to_f(re[j])));
+      }
+    }
+  }
   float acc = 0.f;
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
@@ -129,10 +149,14 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_generic_kernel(co
     return;
   }
   const T* xr = reinterpret_cast<const T*>(a.x + b * a.x_sb + src_t * a.x_ss);
+  const T* rr = a.res ? reinterpret_cast<const T*>(a.res + static_cast<int64_t>(row) * a.res_ss) : nullptr;
+  auto elem = [&](int i) -> T {
+    return rr ? ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(xr[i]), ElemOps<T>::to_f(rr[i]))) : xr[i];
+  };
   float acc = 0.f;
   for (int base = lane * EPV; base < a.H; base += 32 * EPV) {
     for (int j = 0; j < EPV && base + j < a.H; ++j) {
-      const float f = ElemOps<T>::to_f(xr[base + j]);
+      const float f = ElemOps<T>::to_f(elem(base + j));
       acc = __fmaf_rn(f, f, acc);
     }
   }
@@ -143,7 +167,7 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_generic_kernel(co
   T* nr = reinterpret_cast<T*>(a.normed + b * a.o_sb + t * a.o_ss);
   const T* w = reinterpret_cast<const T*>(a.w);
   for (int i = lane; i < a.H; i += 32) {
-    const T xv = xr[i];
+    const T xv = elem(i);
     if (gr) gr[i] = xv;
     nr[i] = norm_elem<T>(ElemOps<T>::to_f(xv), inv, w, i);
   }

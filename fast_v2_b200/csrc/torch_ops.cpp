@@ -400,6 +400,37 @@ void swiglu(const Tensor& gu, const Tensor& out) {
            "swiglu");
 }
 
+// x, res, sum_out, normed: [..., H] with uniformly strided rows.  sum_out
+// may be res itself (in-place residual update) or absent.
+void add_rmsnorm(const Tensor& x, const Tensor& res, const std::optional<Tensor>& weight, double eps,
+                 const std::optional<Tensor>& sum_out, const Tensor& normed) {
+  const int64_t H = x.size(-1);
+  const int64_t rows = x.numel() / H;
+  auto rs = [&](const Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda() && t.dtype() == x.dtype() && t.size(-1) == H && t.numel() / H == rows &&
+                    t.stride(-1) == 1,
+                "fdl.add_rmsnorm: ", name, " must be a CUDA tensor of x's dtype and shape with unit inner stride");
+    for (int64_t d = 0; d + 2 < t.dim(); ++d)
+      TORCH_CHECK(t.stride(d) == t.size(d + 1) * t.stride(d + 1), "fdl.add_rmsnorm: ", name,
+                  " rows must be uniformly strided");
+    return t.dim() >= 2 ? t.stride(-2) : H;
+  };
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf,
+              "fdl.add_rmsnorm: bf16 or fp16 tensors");
+  const int64_t x_rs = rs(x, "x"), r_rs = rs(res, "res"), o_rs = rs(normed, "normed");
+  if (sum_out) TORCH_CHECK(rs(*sum_out, "sum_out") == o_rs, "fdl.add_rmsnorm: sum_out and normed row strides differ");
+  if (weight)
+    TORCH_CHECK(weight->is_cuda() && weight->dim() == 1 && weight->size(0) == H && weight->is_contiguous() &&
+                    weight->dtype() == x.dtype(),
+                "fdl.add_rmsnorm: weight must be a contiguous [H] tensor with x's dtype");
+  c10::cuda::CUDAGuard guard(x.device());
+  check_rc(fdl_add_rmsnorm(x.data_ptr(), x_rs, res.data_ptr(), r_rs, weight ? weight->data_ptr() : nullptr,
+                           static_cast<float>(eps), sum_out ? sum_out->data_ptr() : nullptr, normed.data_ptr(), o_rs,
+                           static_cast<int>(rows), static_cast<int>(H),
+                           x.scalar_type() == at::kBFloat16 ? FDL_BF16 : FDL_F16, cur_stream()),
+           "add_rmsnorm");
+}
+
 // Functional form with the signature of the flash_kvcache custom op of
 // utils/attention_backends.py:83-86; workspace comes from torch's caching
 // allocator (graph-capture safe).
@@ -445,6 +476,7 @@ TORCH_LIBRARY(fdl, m) {
   m.def("rope_qkv(Tensor y, Tensor pos, Tensor inv_freq, int hq, int hkv, Tensor(a!) q, Tensor(b!) k, "
         "Tensor(c!) v) -> ()");
   m.def("swiglu(Tensor gu, Tensor(a!) out) -> ()");
+  m.def("add_rmsnorm(Tensor x, Tensor res, Tensor? weight, float eps, Tensor(a!)? sum_out, Tensor(b!) normed) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
@@ -458,6 +490,7 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("flash_kvcache", &flash_kvcache);
   m.impl("rope_qkv", &rope_qkv);
   m.impl("swiglu", &swiglu);
+  m.impl("add_rmsnorm", &add_rmsnorm);
 }
 
 TORCH_LIBRARY_IMPL(fdl, Meta, m) {
@@ -481,4 +514,6 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
   m.impl("rope_qkv", [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
                         const Tensor&) {});
   m.impl("swiglu", [](const Tensor&, const Tensor&) {});
+  m.impl("add_rmsnorm", [](const Tensor&, const Tensor&, const std::optional<Tensor>&, double,
+                           const std::optional<Tensor>&, const Tensor&) {});
 }

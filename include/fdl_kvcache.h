@@ -230,6 +230,22 @@ int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb,
                        fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Residual add fused with RMSNorm (16-bit dtypes): for each of `rows` rows
+ *     sum[r, :]    = round(x[r, :] + res[r, :])
+ *     normed[r, :] = RMSNorm(sum[r, :]) exactly as fdl_gather_rmsnorm
+ * i.e. the decoder layer's `hidden_states = residual + hidden_states`
+ * followed by post_attention_layernorm / the next layer's input_layernorm
+ * (Qwen2DecoderLayer.forward as used by modeling.py; RMSNorm per
+ * modeling.py:427-432).  Row strides x_rs, res_rs, out_rs in elements;
+ * sum_out and normed share out_rs.  sum_out may alias res (in-place update
+ * of the residual stream); sum_out == NULL skips writing the sum.
+ * ---------------------------------------------------------------------- */
+int fdl_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs,
+                    const void* w, float eps, void* sum_out, void* normed,
+                    int64_t out_rs, int rows, int hidden, int x_dtype,
+                    fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * (d) Block attention of the current query block over the KV cache, with
  * the GQA expansion done in-kernel (tcgen05 / TMEM / TMA, sm_100a).
  *

@@ -206,6 +206,18 @@ def gather_rmsnorm_bf16(x_bits, idx, w_bits, eps: float):
     return g, out
 
 
+def add_rmsnorm_bf16(x_bits, res_bits, w_bits, eps: float):
+    """Decoder-layer residual connection followed by RMSNorm: the layer's
+    `hidden_states = residual + hidden_states` (bf16 + bf16 -> one rounding)
+    and then Fast_dLLM_QwenRMSNorm.forward (modeling.py:427-432) on the sum.
+    Rows are the leading axes.  Returns (sum bits, normed bits)."""
+    sm = f32_to_bf16((bf16_to_f32(x_bits) + bf16_to_f32(res_bits)).astype(np.float32))
+    flat = sm.reshape(1, -1, sm.shape[-1])
+    idx = np.arange(flat.shape[1])[None, :]
+    _, n = gather_rmsnorm_bf16(flat, idx, w_bits, eps)
+    return sm, n.reshape(sm.shape)
+
+
 def gather_rmsnorm_f32(x, idx, w, eps: float):
     """select_gather_rmsnorm_kernel (cuda_bench/fused_gather_norm.cu:123-175):
     fp32 in/out, out = x * rsqrt(mean(x^2) + eps) (* w when given)."""

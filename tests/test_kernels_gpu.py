@@ -214,6 +214,26 @@ def test_gather_rmsnorm_config1_shape():
     assert np.mean(bits_of(normed) != en) < 0.01
 
 
+@pytest.mark.parametrize("rows,H,inplace", [(2048, 3584, True), (37, 3584, False), (5, 1000, True)])
+def test_add_rmsnorm_matches_residual_then_norm(rows, H, inplace):
+    """Residual add + RMSNorm: the sum is bit-exact (one bf16 rounding), the
+    normed rows match the oracle like gather_rmsnorm; in place over the
+    residual stream as the decode forward uses it (H = 1000 takes the generic
+    scalar path)."""
+    x, res = rbf16((rows, H), 61), rbf16((rows, H), 62)
+    w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16)
+    es, en = O.add_rmsnorm_bf16(bits_of(x), bits_of(res), bits_of(w), 1e-6)
+    dx, dres, dw = x.to(DEV), res.to(DEV), w.to(DEV)
+    normed = torch.empty_like(dx)
+    sum_out = dres if inplace else torch.empty_like(dx)
+    torch.ops.fdl.add_rmsnorm(dx, dres, dw, 1e-6, sum_out, normed)
+    assert np.array_equal(bits_of(sum_out), es)
+    assert_close("add_rmsnorm", normed.float().cpu().numpy(), O.bf16_to_f32(en), ATOL, RTOL)
+    assert np.mean(bits_of(normed) != en) < 0.01
+    # torch's own bf16 add is the reference's residual connection
+    assert torch.equal(sum_out.cpu(), x + res)
+
+
 # ------------------------------------------------------------------ (d)
 def _run_attn(q, k, v, seqlens, splits=0, kb=None, vb=None, mask_block=0, q_pos=None):
     out = torch.empty_like(q)
@@ -332,3 +352,18 @@ def test_swiglu_matches_reference_rounding():
     tg = gu.to(DEV)
     t = torch.nn.functional.silu(tg[:, :F_]) * tg[:, F_:]
     assert torch.mean((t != out).float()).item() < 2e-3
+
+
+def test_swiglu_exhaustive_gate_values():
+    """The fast silu path with its rounding-midpoint guard gives torch's
+    bf16 silu for every one of the 65536 bf16 gate values (up = 1)."""
+    F_ = 65536
+    gate = torch.arange(F_, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    gu = torch.cat([gate, torch.ones(F_, dtype=torch.bfloat16)]).view(1, 2 * F_).to(DEV)
+    out = torch.empty(1, F_, dtype=torch.bfloat16, device=DEV)
+    torch.ops.fdl.swiglu(gu, out)
+    ref = torch.nn.functional.silu(gu[:, :F_])
+    a, b = out.view(torch.int16), ref.view(torch.int16)
+    both_nan = torch.isnan(out) & torch.isnan(ref)
+    bad = (a != b) & ~both_nan
+    assert int(bad.sum()) == 0, gate[bad[0].cpu()][:8]
