@@ -399,12 +399,20 @@ def _e2e(args, rank, world, kt, geo_name):
     B = args.e2e_batch or B
     cpu_only = getattr(args, "impl", "ours") == "reference"
     model = None if cpu_only else BlockDiffusionLM(geo, device="cuda", seed=100 + rank)
+    if model is not None:
+        # Random weights can put the mask token on top of the argmax, which a
+        # trained model never does (and which stalls the reference's unmask
+        # loop); its lm_head row is zeroed so its logit stays below the max.
+        from fast_v2_b200.block_decode import MASK_ID
+
+        model.lm_head[MASK_ID].zero_()
     meta = dict(
         metric=f"generated tokens/s ({geo_name.upper()} geometry, bs{B}/GPU, block-diffusion decode)",
         unit="tokens/s", dtype="bf16",
         config={"workload": f"e2e_{geo_name}", "model": f"Qwen2.5-{geo_name.upper()} geometry, random init",
                 "params": param_count(geo), "batch_per_gpu": B, "prompt": P, "gen": G, "block": 32, "sub_block": 8,
                 "threshold": 0.9, "cache": cache_desc, "step": "one 32-token block (diffusion steps + commit)",
+                "weights": "random normal(0, 0.02); lm_head row of the mask token zeroed",
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
                                                       use_graphs=True)

@@ -468,6 +468,11 @@ class BlockDiffusionDecoder:
             self.src_idx.copy_(self._srcs[sb])
             s, e = sb * self.sub, (sb + 1) * self.sub
             while bool((self.x[:, s:e] == self.mask_id).any()):
+                # Every step unmasks at least one position unless the model
+                # predicts the mask token itself (then the reference's loop
+                # never ends); fail loudly instead of spinning.
+                if n_fwd >= 4 * blk:
+                    raise RuntimeError("block decode made no progress: the model keeps predicting the mask token")
                 if step_in_block <= 1 or step_in_block % self.refresh == 0:
                     self._run("full")
                 else:

@@ -1,7 +1,7 @@
 // (c) Fused gather + RMSNorm.  One warp per output row: the gathered row is
 // loaded once into registers with 16-byte loads (VPL vectors per lane), the
-// sum of squares is accumulated in fp32 (per-lane sequential FMA, then an
-// xor-butterfly), and both outputs (the gathered copy and the normalised row)
+// sum of squares is accumulated in fp32 (per lane, two sequential FMA chains
+// over alternating vectors, then an xor-butterfly), and both outputs (the gathered copy and the normalised row)
 // are written from registers -- one HBM read and one or two HBM writes per
 // element, nothing else.
 #pragma once
@@ -58,58 +58,76 @@ __device__ __forceinline__ T norm_elem(float x, float inv, const T* w, int i) {
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __grid_constant__ NormArgs a) {
   constexpr int EPV = 16 / sizeof(T);  // elements per 16-byte vector
+  // The weight row is staged once per CTA in shared memory (the four rows of
+  // the CTA share it), so the output phase reads it at shared-memory latency
+  // without holding it in registers through the reduction.
+  __shared__ uint4 w_s[32 * VPL];
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
-  if (row >= a.B * a.T) return;
-  const int b = row / a.T;
-  const int t = row - b * a.T;
-  int64_t src_t = a.idx ? a.idx[b * a.idx_sb + t] : t;
-  if (src_t < 0 || src_t >= a.S) {
-    if (lane == 0) report(FDL_DEV_INDEX, src_t);
-    return;
-  }
-  const char* xr = a.x + b * a.x_sb + src_t * a.x_ss;
   const int nvec = a.H / EPV;
-  uint4 v[VPL];
-#pragma unroll
-  for (int k = 0; k < VPL; ++k) {
-    const int vi = lane + 32 * k;
-    if (vi < nvec) v[k] = ld_stream16(xr + vi * 16);
+  if (a.w)
+    for (int i = threadIdx.x; i < nvec; i += kNormThreads) w_s[i] = *reinterpret_cast<const uint4*>(a.w + i * 16);
+  bool live = row < a.B * a.T;
+  int b = 0, t = 0;
+  int64_t src_t = 0;
+  if (live) {
+    b = row / a.T;
+    t = row - b * a.T;
+    src_t = a.idx ? a.idx[b * a.idx_sb + t] : t;
+    if (src_t < 0 || src_t >= a.S) {
+      if (lane == 0) report(FDL_DEV_INDEX, src_t);
+      live = false;
+    }
   }
-  if (a.res) {
-    // Residual connection (decoder layer `residual + hidden_states`): one
-    // rounding to the storage dtype, then the norm of the rounded sum.
-    const char* rr = a.res + static_cast<int64_t>(row) * a.res_ss;
+  uint4 v[VPL];
+  float acc = 0.f;
+  if (live) {
+    const char* xr = a.x + b * a.x_sb + src_t * a.x_ss;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int vi = lane + 32 * k;
+      if (vi < nvec) v[k] = ld_stream16(xr + vi * 16);
+    }
+    if (a.res) {
+      // Residual connection (decoder layer `residual + hidden_states`): one
+      // rounding to the storage dtype, then the norm of the rounded sum.
+      const char* rr = a.res + static_cast<int64_t>(row) * a.res_ss;
+#pragma unroll
+      for (int k = 0; k < VPL; ++k) {
+        const int vi = lane + 32 * k;
+        if (vi < nvec) {
+          // plain load: the sum may be written back over the residual in place
+          const uint4 rv = *reinterpret_cast<const uint4*>(rr + vi * 16);
+          T* e = reinterpret_cast<T*>(&v[k]);
+          const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+          for (int j = 0; j < EPV; ++j)
+            e[j] = ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(e[j]), ElemOps<T>::to_f(re[j])));
+        }
+      }
+    }
+    // Two independent FMA chains (even / odd vectors of the lane) halve the
+    // dependent-latency chain; the generic kernel uses the same order.
+    float acc2[2] = {0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
       const int vi = lane + 32 * k;
       if (vi < nvec) {
-        // plain load: the sum may be written back over the residual in place
-        const uint4 rv = *reinterpret_cast<const uint4*>(rr + vi * 16);
-        T* e = reinterpret_cast<T*>(&v[k]);
-        const T* re = reinterpret_cast<const T*>(&rv);
+        const T* e = reinterpret_cast<const T*>(&v[k]);
 #pragma unroll
-        for (int j = 0; j < EPV; ++j)
-          e[j] = ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(e[j]), ElemOps<T>::to_f(re[j])));
+        for (int j = 0; j < EPV; ++j) {
+          const float f = ElemOps<T>::to_f(e[j]);
+          acc2[k & 1] = __fmaf_rn(f, f, acc2[k & 1]);
+        }
       }
     }
-  }
-  float acc = 0.f;
-#pragma unroll
-  for (int k = 0; k < VPL; ++k) {
-    const int vi = lane + 32 * k;
-    if (vi < nvec) {
-      const T* e = reinterpret_cast<const T*>(&v[k]);
-#pragma unroll
-      for (int j = 0; j < EPV; ++j) {
-        const float f = ElemOps<T>::to_f(e[j]);
-        acc = __fmaf_rn(f, f, acc);
-      }
-    }
+    acc = __fadd_rn(acc2[0], acc2[1]);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
   const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(a.H)), a.eps));
+  __syncthreads();  // w_s complete
+  if (!live) return;
 
   char* gr = a.gathered ? a.gathered + b * a.o_sb + t * a.o_ss : nullptr;
   char* nr = a.normed + b * a.o_sb + t * a.o_ss;
@@ -119,9 +137,7 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
     if (vi < nvec) {
       if (gr) st_stream16(gr + vi * 16, v[k]);
       const T* e = reinterpret_cast<const T*>(&v[k]);
-      // One 16-byte weight load per vector (L1/L2 resident across rows).
-      uint4 wv;
-      if (a.w) wv = *reinterpret_cast<const uint4*>(a.w + vi * 16);
+      const uint4 wv = a.w ? w_s[vi] : make_uint4(0, 0, 0, 0);
       const T* we = reinterpret_cast<const T*>(&wv);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
@@ -153,13 +169,15 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_generic_kernel(co
   auto elem = [&](int i) -> T {
     return rr ? ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(xr[i]), ElemOps<T>::to_f(rr[i]))) : xr[i];
   };
-  float acc = 0.f;
-  for (int base = lane * EPV; base < a.H; base += 32 * EPV) {
+  float acc2[2] = {0.f, 0.f};
+  int chunk = 0;
+  for (int base = lane * EPV; base < a.H; base += 32 * EPV, ++chunk) {
     for (int j = 0; j < EPV && base + j < a.H; ++j) {
       const float f = ElemOps<T>::to_f(elem(base + j));
-      acc = __fmaf_rn(f, f, acc);
+      acc2[chunk & 1] = __fmaf_rn(f, f, acc2[chunk & 1]);
     }
   }
+  float acc = __fadd_rn(acc2[0], acc2[1]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
   const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(acc, static_cast<float>(a.H)), a.eps));
