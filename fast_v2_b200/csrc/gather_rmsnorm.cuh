@@ -5,7 +5,9 @@
 // are written from registers -- one HBM read and one or two HBM writes per
 // element, nothing else.
 #pragma once
+#include <type_traits>
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace fdl {
 
@@ -98,30 +100,73 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
         if (vi < nvec) {
           // plain load: the sum may be written back over the residual in place
           const uint4 rv = *reinterpret_cast<const uint4*>(rr + vi * 16);
-          T* e = reinterpret_cast<T*>(&v[k]);
-          const T* re = reinterpret_cast<const T*>(&rv);
+          if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+            // bf16x2 add: the exact sum rounded once, equal to the fp32 sum
+            // rounded to bf16 (the fp32 rounding of a sum of two bf16 values
+            // never lands on a bf16 midpoint the exact sum is not on).
+            __nv_bfloat162* e2 = reinterpret_cast<__nv_bfloat162*>(&v[k]);
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
 #pragma unroll
-          for (int j = 0; j < EPV; ++j)
-            e[j] = ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(e[j]), ElemOps<T>::to_f(re[j])));
+            for (int j = 0; j < 4; ++j) e2[j] = __hadd2(e2[j], r2[j]);
+          } else {
+            T* e = reinterpret_cast<T*>(&v[k]);
+            const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+            for (int j = 0; j < EPV; ++j)
+              e[j] = ElemOps<T>::from_f(__fadd_rn(ElemOps<T>::to_f(e[j]), ElemOps<T>::to_f(re[j])));
+          }
         }
       }
     }
-    // Two independent FMA chains (even / odd vectors of the lane) halve the
-    // dependent-latency chain; the generic kernel uses the same order.
-    float acc2[2] = {0.f, 0.f};
+    // The gathered copy (or the residual sum) is final now: store it before
+    // the reduction so the writes overlap the arithmetic.
+    if (a.gathered) {
+      char* gr = a.gathered + b * a.o_sb + t * a.o_ss;
 #pragma unroll
-    for (int k = 0; k < VPL; ++k) {
-      const int vi = lane + 32 * k;
-      if (vi < nvec) {
-        const T* e = reinterpret_cast<const T*>(&v[k]);
-#pragma unroll
-        for (int j = 0; j < EPV; ++j) {
-          const float f = ElemOps<T>::to_f(e[j]);
-          acc2[k & 1] = __fmaf_rn(f, f, acc2[k & 1]);
-        }
+      for (int k = 0; k < VPL; ++k) {
+        const int vi = lane + 32 * k;
+        if (vi < nvec) st_stream16(gr + vi * 16, v[k]);
       }
     }
-    acc = __fadd_rn(acc2[0], acc2[1]);
+    if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+      // Packed: a bf16 pair widens to two floats with two integer ops, and one
+      // f32x2 FMA accumulates both; four chains (element parity x vector
+      // parity) per lane.
+      uint64_t acc2[2] = {0, 0};
+#pragma unroll
+      for (int k = 0; k < VPL; ++k) {
+        const int vi = lane + 32 * k;
+        if (vi < nvec) {
+          const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[k]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t f2 = ptx::pack2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xFFFF0000u));
+            acc2[k & 1] = ptx::fma2(f2, f2, acc2[k & 1]);
+          }
+        }
+      }
+      float a0, a1, a2, a3;
+      ptx::unpack2(acc2[0], a0, a1);
+      ptx::unpack2(acc2[1], a2, a3);
+      acc = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+    } else {
+      // Two independent FMA chains (even / odd vectors of the lane); the
+      // generic kernel uses the same order.
+      float acc2[2] = {0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < VPL; ++k) {
+        const int vi = lane + 32 * k;
+        if (vi < nvec) {
+          const T* e = reinterpret_cast<const T*>(&v[k]);
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) {
+            const float f = ElemOps<T>::to_f(e[j]);
+            acc2[k & 1] = __fmaf_rn(f, f, acc2[k & 1]);
+          }
+        }
+      }
+      acc = __fadd_rn(acc2[0], acc2[1]);
+    }
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
@@ -129,20 +174,38 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
   __syncthreads();  // w_s complete
   if (!live) return;
 
-  char* gr = a.gathered ? a.gathered + b * a.o_sb + t * a.o_ss : nullptr;
   char* nr = a.normed + b * a.o_sb + t * a.o_ss;
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int vi = lane + 32 * k;
     if (vi < nvec) {
-      if (gr) st_stream16(gr + vi * 16, v[k]);
-      const T* e = reinterpret_cast<const T*>(&v[k]);
       const uint4 wv = a.w ? w_s[vi] : make_uint4(0, 0, 0, 0);
-      const T* we = reinterpret_cast<const T*>(&wv);
       uint4 o;
-      T* oe = reinterpret_cast<T*>(&o);
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        // Per pair: f32x2 multiply by inv, one packed rounding to bf16 (the
+        // reference's fp32 product then .to(bf16)), then w * n as a bf16x2
+        // multiply -- the exact product rounded once, which is what the
+        // reference's bf16 * bf16 (fp32 multiply, exact for 8-bit
+        // mantissas, then rounding) gives.
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[k]);
+        const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+        const uint64_t inv2 = ptx::pack2(inv, inv);
 #pragma unroll
-      for (int j = 0; j < EPV; ++j) oe[j] = norm_elem<T>(ElemOps<T>::to_f(e[j]), inv, a.w ? we : nullptr, j);
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t f2 = ptx::pack2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xFFFF0000u));
+          float n0, n1;
+          ptx::unpack2(ptx::mul2(f2, inv2), n0, n1);
+          const __nv_bfloat162 n = __floats2bfloat162_rn(n0, n1);
+          o2[j] = a.w ? __hmul2(w2[j], n) : n;
+        }
+      } else {
+        const T* e = reinterpret_cast<const T*>(&v[k]);
+        const T* we = reinterpret_cast<const T*>(&wv);
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) oe[j] = norm_elem<T>(ElemOps<T>::to_f(e[j]), inv, a.w ? we : nullptr, j);
+      }
       st_stream16(nr + vi * 16, o);
     }
   }
