@@ -17,10 +17,10 @@
 // Per key tile j and row tile m:
 //   S_m = Q_m K_j^T          tcgen05.mma, A and B from shared memory,
 //                            128 fp32 TMEM columns
-//   softmax warps            S_m row loaded into registers (one TMEM wait),
-//                            row max, then P = exp2(S - max) written back as
-//                            bf16 into the first 64 columns of S_m's own
-//                            TMEM range;
+//   softmax warps            S_m row read from TMEM in halves of 64
+//                            columns (no register spills), row max, then
+//                            P = exp2(S - max) written back as bf16 into the
+//                            first 64 columns of S_m's own TMEM range;
 //                            O_m is rescaled in TMEM only when the row max
 //                            grows by more than 2^8 (the stale max is kept
 //                            otherwise -- identical up to rounding)
@@ -51,10 +51,6 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + m * 128
 constexpr uint32_t kTmemO = 256;  // + m * 128
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
-#ifndef FDL_ATTN_EMU_PAIRS
-#define FDL_ATTN_EMU_PAIRS 0
-#endif
-constexpr int kEmuPairs = FDL_ATTN_EMU_PAIRS;
 #ifndef FDL_ATTN_PREFETCH
 #define FDL_ATTN_PREFETCH 1
 #endif
@@ -358,38 +354,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
       // Visible keys of this tile for this row form a prefix of the tile.
       const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : 0;
-      // The whole S row (128 fp32 columns) is loaded with four back-to-back
-      // TMEM loads and a single wait, then kept in registers.
-      float sv0[32], sv1[32], sv2[32], sv3[32];
-      ptx::tmem_ld32(t_s + 0, sv0);
-      ptx::tmem_ld32(t_s + 32, sv1);
-      ptx::tmem_ld32(t_s + 64, sv2);
-      ptx::tmem_ld32(t_s + 96, sv3);
-      ptx::tmem_wait_ld();
-      // Tiles with every key visible to every row of the warp (all but the
-      // sequence's last tiles) take the unpredicated path.
+      // The S row is read in halves of 64 columns so no more than 64 values
+      // are live: the upper half (keys 64..127) is read first for its max,
+      // then the lower half, which stays in registers; after the lower
+      // half's P is written (over S columns 0..31, already consumed) the
+      // upper half is read again.
       const bool full = __all_sync(0xffffffffu, climit == kBlockN);
-      float tmax;
-      if (full) {
-        float a0 = sv0[0], a1 = sv1[0], a2 = sv2[0], a3 = sv3[0];
+      float sa[32], sb[32];
+      // Max of 64 columns [c0, c0 + 64) held in lo / hi.
+      auto half_max = [&](const float (&lo)[32], const float (&hi)[32], int c0) {
+        float mx = -INFINITY;
+        if (full) {
+          float a0 = lo[0], a1 = hi[0];
 #pragma unroll
-        for (int i = 1; i < 31; i += 2) {
-          a0 = ptx::fmax3(a0, sv0[i], sv0[i + 1]);
-          a1 = ptx::fmax3(a1, sv1[i], sv1[i + 1]);
-          a2 = ptx::fmax3(a2, sv2[i], sv2[i + 1]);
-          a3 = ptx::fmax3(a3, sv3[i], sv3[i + 1]);
-        }
-        tmax = ptx::fmax3(ptx::fmax3(a0, a1, sv0[31]), ptx::fmax3(a2, a3, sv1[31]), fmaxf(sv2[31], sv3[31]));
-      } else {
-        tmax = -INFINITY;
+          for (int i = 1; i < 31; i += 2) {
+            a0 = ptx::fmax3(a0, lo[i], lo[i + 1]);
+            a1 = ptx::fmax3(a1, hi[i], hi[i + 1]);
+          }
+          mx = ptx::fmax3(a0, a1, fmaxf(lo[31], hi[31]));
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < climit) tmax = fmaxf(tmax, sv0[i]);
-          if (32 + i < climit) tmax = fmaxf(tmax, sv1[i]);
-          if (64 + i < climit) tmax = fmaxf(tmax, sv2[i]);
-          if (96 + i < climit) tmax = fmaxf(tmax, sv3[i]);
+          for (int i = 0; i < 32; ++i) {
+            if (c0 + i < climit) mx = fmaxf(mx, lo[i]);
+            if (c0 + 32 + i < climit) mx = fmaxf(mx, hi[i]);
+          }
         }
-      }
+        return mx;
+      };
+      ptx::tmem_ld32(t_s + 64, sa);
+      ptx::tmem_ld32(t_s + 96, sb);
+      ptx::tmem_wait_ld();
+      float tmax = half_max(sa, sb, 64);
+      ptx::tmem_ld32(t_s + 0, sa);
+      ptx::tmem_ld32(t_s + 32, sb);
+      ptx::tmem_wait_ld();
+      tmax = fmaxf(tmax, half_max(sa, sb, 0));
       tmax *= p.scale_log2;  // scale > 0: max commutes with the scaling
       const float m_new = fmaxf(m_used, tmax);
       const bool grow = m_new > m_used + 8.f;  // true on the first finite max
@@ -415,9 +414,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       float rsum = 0.f;
       const float neg_m = -m_used;
       if (full) {
-        // Packed pairs: x = S * scale - max by one f32x2 FMA; kEmuPairs of
-        // every 8 pairs take 2^x from the FMA-pipe polynomial, the rest from
-        // the special-function unit, so the two units share the exponentials.
+        // Packed pairs: x = S * scale - max by one f32x2 FMA, 2^x from the
+        // special-function unit, the row sum by f32x2 adds.
         const uint64_t sc2 = ptx::pack2(p.scale_log2, p.scale_log2);
         const uint64_t nm2 = ptx::pack2(neg_m, neg_m);
         uint64_t acc2 = ptx::pack2(0.f, 0.f);
@@ -426,14 +424,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-            uint64_t e2;
-            if ((i & 7) < kEmuPairs) {
-              e2 = ptx::exp2_poly2(x2);
-            } else {
-              float x0, x1;
-              ptx::unpack2(x2, x0, x1);
-              e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
-            }
+            float x0, x1;
+            ptx::unpack2(x2, x0, x1);
+            const uint64_t e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
             acc2 = ptx::add2(acc2, e2);
             float p0, p1;
             ptx::unpack2(e2, p0, p1);
@@ -442,10 +435,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           }
           ptx::tmem_st16(t_s + c * 16, pk);
         };
-        emit_full(sv0, 0);
-        emit_full(sv1, 1);
-        emit_full(sv2, 2);
-        emit_full(sv3, 3);
+        emit_full(sa, 0);
+        emit_full(sb, 1);
+        ptx::tmem_ld32(t_s + 64, sa);
+        ptx::tmem_ld32(t_s + 96, sb);
+        ptx::tmem_wait_ld();
+        emit_full(sa, 2);
+        emit_full(sb, 3);
         float s0, s1;
         ptx::unpack2(acc2, s0, s1);
         rsum = s0 + s1;
@@ -463,10 +459,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           }
           ptx::tmem_st16(t_s + c * 16, pk);
         };
-        emit(sv0, 0);
-        emit(sv1, 1);
-        emit(sv2, 2);
-        emit(sv3, 3);
+        emit(sa, 0);
+        emit(sb, 1);
+        ptx::tmem_ld32(t_s + 64, sa);
+        ptx::tmem_ld32(t_s + 96, sb);
+        ptx::tmem_wait_ld();
+        emit(sa, 2);
+        emit(sb, 3);
       }
       l += rsum;
       ptx::tmem_wait_st();

@@ -69,7 +69,7 @@ bool attn_smem_configured() {
 // tile for the combine pass when split.  One CTA per SM.
 int pick_splits(int work_items, int tiles_est) {
   const int sms = num_sms();
-  const int max_s = std::min(64, std::max(1, tiles_est / 2));
+  const int max_s = std::min(64, std::max(1, tiles_est));
   int best = 1;
   int64_t best_cost = INT64_MAX;
   for (int s = 1; s <= max_s; ++s) {

@@ -241,32 +241,5 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for two lanes on the FMA pipe instead of the special-function unit.
-// Range reduction x = n + f with n = round(x) (the 1.5 * 2^23 shift leaves n
-// in the low mantissa bits), f in [-1/2, 1/2]; 2^f from a cubic fitted here
-// to minimise the relative error on that interval (max relative error
-// 7.5e-5, far below the bf16 rounding the result receives); 2^n is added to
-// the exponent field.  Inputs are clamped to >= -125 so the exponent never
-// underflows (2^-125 is zero at the softmax's bf16 precision).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261093f, c3 = 0.055171646f;
-  float x0, x1;
-  unpack2(x, x0, x1);
-  x = pack2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const uint64_t shift = pack2(kShift, kShift);
-  const uint64_t t = add2(x, shift);
-  const uint64_t f = sub2(x, sub2(t, shift));
-  uint64_t pl = fma2(f, pack2(c3, c3), pack2(c2, c2));
-  pl = fma2(pl, f, pack2(c1, c1));
-  pl = fma2(pl, f, pack2(c0, c0));
-  uint32_t p0, p1, t0, t1;
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(p0), "=r"(p1) : "l"(pl));
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(p0 + (t0 << 23)), "r"(p1 + (t1 << 23)));
-  return r;
-}
-
 }  // namespace ptx
 }  // namespace fdl
