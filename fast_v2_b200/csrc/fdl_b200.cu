@@ -135,10 +135,10 @@ int fdl_kv_scatter(void* k_dst, void* v_dst, const void* k_src, const void* v_sr
                    int64_t pos_sb, int batch, int n, int dst_len, int heads, int head_dim, int elem_bytes,
                    int64_t dst_sb, int64_t dst_ss, int64_t dst_sh, int64_t src_sb, int64_t src_ss, int64_t src_sh,
                    fdl_stream_t stream) {
-  if (!k_dst || !k_src || !pos || (v_dst && !v_src)) return FDL_E_NULL;
   if (batch < 1 || batch > 65535 || n < 0 || dst_len < 1 || heads < 1 || head_dim < 1) return FDL_E_SHAPE;
   if (elem_bytes != 2 && elem_bytes != 4) return FDL_E_DTYPE;
   if (n == 0) return FDL_OK;
+  if (!k_dst || !k_src || !pos || (v_dst && !v_src)) return FDL_E_NULL;
   ScatterArgs a{};
   const int64_t rb = static_cast<int64_t>(head_dim) * elem_bytes;
   a.dst[0] = static_cast<char*>(k_dst);
@@ -173,11 +173,13 @@ int fdl_kv_gather_prefix(const void* k_prefix, const void* v_prefix, const int32
                          const int32_t* cu_seqlens, int batch, int heads, int head_dim, int rep, int elem_bytes,
                          int64_t pre_sb, int64_t pre_ss, int64_t pre_sh, int64_t blk_sb, int64_t blk_ss,
                          int64_t blk_sh, int64_t out_sb, int64_t out_ss, int64_t out_sh, fdl_stream_t stream) {
-  if (!k_prefix || !k_out || !len || (v_out && !v_prefix)) return FDL_E_NULL;
-  if (n_blk > 0 && (!k_block || (v_out && !v_block))) return FDL_E_NULL;
   if (batch < 1 || batch > 65535 || prefix_cap < 0 || n_blk < 0 || heads < 1 || head_dim < 1 || rep < 1)
     return FDL_E_SHAPE;
   if (elem_bytes != 2 && elem_bytes != 4) return FDL_E_DTYPE;
+  if (prefix_cap + n_blk == 0) return FDL_OK;
+  if (!len || (!k_out && !v_out)) return FDL_E_NULL;
+  if (!k_prefix || !k_out || (v_out && !v_prefix)) return FDL_E_NULL;
+  if (n_blk > 0 && (!k_block || (v_out && !v_block))) return FDL_E_NULL;
   GatherPrefixArgs a{};
   const int64_t rb = static_cast<int64_t>(head_dim) * elem_bytes;
   a.pre[0] = static_cast<const char*>(k_prefix);
@@ -217,10 +219,10 @@ int fdl_kv_gather_rows(const void* k_src, const void* v_src, const void* idx, in
                        const int32_t* count, void* k_out, void* v_out, int batch, int n, int src_len, int heads,
                        int head_dim, int elem_bytes, int64_t src_sb, int64_t src_ss, int64_t src_sh, int64_t out_sb,
                        int64_t out_ss, int64_t out_sh, fdl_stream_t stream) {
-  if (!k_src || !k_out || !idx || (v_out && !v_src)) return FDL_E_NULL;
   if (batch < 1 || batch > 65535 || n < 0 || src_len < 1 || heads < 1 || head_dim < 1) return FDL_E_SHAPE;
   if (elem_bytes != 2 && elem_bytes != 4) return FDL_E_DTYPE;
   if (n == 0) return FDL_OK;
+  if (!k_src || !k_out || !idx || (v_out && !v_src)) return FDL_E_NULL;
   GatherRowsArgs a{};
   const int64_t rb = static_cast<int64_t>(head_dim) * elem_bytes;
   a.src[0] = static_cast<const char*>(k_src);
@@ -331,11 +333,11 @@ int fdl_kv_sparse_prefix_noalloc(const void* k, const void* v, const int32_t* le
 int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb, const void* w, float eps, void* gathered,
                        void* normed, int batch, int seq, int n_tok, int hidden, int x_dtype, int64_t x_sb,
                        int64_t x_ss, int64_t out_sb, int64_t out_ss, fdl_stream_t stream) {
-  if (!x || !normed) return FDL_E_NULL;
-  if (batch < 1 || seq < 1 || n_tok < 0 || hidden < 1) return FDL_E_SHAPE;
+  if (batch < 1 || seq < 0 || n_tok < 0 || hidden < 1) return FDL_E_SHAPE;
   if (!idx && n_tok > seq) return FDL_E_SHAPE;
   if (static_cast<int64_t>(batch) * n_tok >= (1ll << 31)) return FDL_E_SHAPE;
   if (n_tok == 0) return FDL_OK;
+  if (!x || !normed) return FDL_E_NULL;
   int es;
   switch (x_dtype) {
     case FDL_BF16: case FDL_F16: es = 2; break;
@@ -367,9 +369,9 @@ int fdl_gather_rmsnorm(const void* x, const int64_t* idx, int64_t idx_sb, const 
 int fdl_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs, const void* w, float eps,
                     void* sum_out, void* normed, int64_t out_rs, int rows, int hidden, int x_dtype,
                     fdl_stream_t stream) {
-  if (!x || !res || !normed) return FDL_E_NULL;
   if (rows < 0 || hidden < 1) return FDL_E_SHAPE;
   if (rows == 0) return FDL_OK;
+  if (!x || !res || !normed) return FDL_E_NULL;
   int es;
   switch (x_dtype) {
     case FDL_BF16: case FDL_F16: es = 2; break;
@@ -498,10 +500,10 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
 
 int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* inv_freq, void* q, void* k, void* v,
                  int rows, int hq, int hkv, int head_dim, fdl_stream_t stream) {
-  if (!y || !pos || !inv_freq || !q || !k || !v) return FDL_E_NULL;
   if (rows < 0 || hq < 1 || hkv < 1 || head_dim < 16 || head_dim % 16 || head_dim / 2 > kRopeMaxHalf)
     return FDL_E_SHAPE;
   if (rows == 0) return FDL_OK;
+  if (!y || !pos || !inv_freq || !q || !k || !v) return FDL_E_NULL;
   if (!aligned16(y) || !aligned16(q) || !aligned16(k) || !aligned16(v) || (y_rs * 2) % 16) return FDL_E_ALIGN;
   RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
              static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), rows, hq, hkv, head_dim};
@@ -511,9 +513,9 @@ int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* i
 
 int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int64_t rows, int ffn,
                fdl_stream_t stream) {
-  if (!gu || !out) return FDL_E_NULL;
   if (rows < 0 || rows > INT32_MAX || ffn < 8 || ffn % 8) return FDL_E_SHAPE;
   if (rows == 0) return FDL_OK;
+  if (!gu || !out) return FDL_E_NULL;
   if (!aligned16(gu) || !aligned16(out) || (gu_rs * 2) % 16 || (out_rs * 2) % 16) return FDL_E_ALIGN;
   SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn};
   const dim3 grid(static_cast<unsigned>(rows), (ffn / 8 + kSwigluChunk - 1) / kSwigluChunk);

@@ -152,6 +152,7 @@ void kv_gather_prefix(const Tensor& k_prefix, const Tensor& v_prefix, const Tens
   for (const Tensor* t : {&k_prefix, &v_prefix, &k_out, &v_out}) check_cuda(*t, "gather tensor");
   TORCH_CHECK(lens.is_cuda() && lens.scalar_type() == at::kInt && lens.is_contiguous(),
               "fdl.kv_gather_prefix: lens must be a contiguous CUDA int32 [B] tensor");
+  if (k_out.numel() == 0) return;  // every sequence empty: nothing to write
   const Rows p = rows_of(k_prefix, seq_dim_in);
   TORCH_CHECK(v_prefix.sizes() == k_prefix.sizes() && v_prefix.strides() == k_prefix.strides(),
               "fdl.kv_gather_prefix: V prefix must match K prefix");

@@ -32,7 +32,9 @@ extern "C" {
 
 typedef struct CUstream_st* fdl_stream_t; /* == cudaStream_t */
 
-/* Host-side argument errors (return values > 0). */
+/* Host-side argument errors (return values > 0).  A call whose sizes
+ * describe no work (zero tokens, rows or positions) returns FDL_OK before
+ * its data pointers are looked at, so empty buffers may be passed as NULL. */
 #define FDL_OK              0
 #define FDL_E_NULL          1  /* required pointer is NULL                     */
 #define FDL_E_SHAPE         2  /* size out of supported range                  */
