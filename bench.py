@@ -413,9 +413,10 @@ def _e2e(args, rank, world, kt, geo_name):
                 "params": param_count(geo), "batch_per_gpu": B, "prompt": P, "gen": G, "block": 32, "sub_block": 8,
                 "threshold": 0.9, "cache": cache_desc, "step": "one 32-token block (diffusion steps + commit)",
                 "weights": "random normal(0, 0.02); lm_head row of the mask token zeroed",
+                "fed_bucket": getattr(args, "fed_bucket", 1),
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
-                                                      use_graphs=True)
+                                                      fed_bucket=args.fed_bucket, use_graphs=True)
     g = gen(4000 + rank)
     if not cpu_only:
         prompt = torch.randint(0, 151643, (B, P), generator=g).cuda()
@@ -577,6 +578,8 @@ def main():
     ap.add_argument("--attn-p", type=int, default=8192)
     ap.add_argument("--attn-sq", type=int, default=32)
     ap.add_argument("--e2e-batch", type=int, default=0)
+    ap.add_argument("--fed-bucket", type=int, default=1,
+                    help="cached dKV steps run at the fed width rounded up to this multiple (1 = exact, as the reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:

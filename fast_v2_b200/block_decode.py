@@ -329,7 +329,7 @@ class BlockDiffusionDecoder:
 
     def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
                  sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
-                 fed_bucket: int = 8, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
+                 fed_bucket: int = 1, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
                  use_graphs: bool = False):
         assert prompt_len % block == 0 and block % sub_block == 0
         self.m, self.B, self.block, self.sub = model, batch, block, sub_block
