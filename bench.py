@@ -323,7 +323,7 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
     from fast_v2_b200 import _lib, ensure_ops
 
     ensure_ops()
-    B, P, Sq, Hq, Hkv, D = args.attn_b, args.attn_p, args.attn_sq, 28, 4, 128
+    B, P, Sq, Hq, Hkv, D = args.attn_b, args.attn_p, args.attn_sq, args.attn_hq, args.attn_hkv, 128
     cap = P + 32
     g = gen(3000 + rank)
     kv_bytes = B * cap * Hkv * D * 2 * 2
@@ -333,7 +333,7 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
     q = (torch.randn(B, Sq, Hq, D, generator=g) / math.sqrt(D)).to(torch.bfloat16).cuda()
     seq = torch.full((B,), cap, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
-    splits = _lib.attn_auto_splits(B, Sq, Hq, Hkv, cap, 0)
+    splits = args.attn_splits or _lib.attn_auto_splits(B, Sq, Hq, Hkv, cap, 0)
     wsb = _lib.attn_workspace_bytes(B, Sq, Hq, splits)
     ws = torch.empty(max(1, wsb), dtype=torch.uint8, device="cuda")
     flops = 4 * B * Hq * Sq * cap * D
@@ -416,7 +416,7 @@ def _e2e(args, rank, world, kt, geo_name):
                 "fed_bucket": getattr(args, "fed_bucket", 1),
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
-                                                      fed_bucket=args.fed_bucket, use_graphs=True)
+                                                      fed_bucket=getattr(args, "fed_bucket", 1), use_graphs=True)
     g = gen(4000 + rank)
     if not cpu_only:
         prompt = torch.randint(0, 151643, (B, P), generator=g).cuda()
@@ -577,6 +577,9 @@ def main():
     ap.add_argument("--attn-b", type=int, default=64)
     ap.add_argument("--attn-p", type=int, default=8192)
     ap.add_argument("--attn-sq", type=int, default=32)
+    ap.add_argument("--attn-hq", type=int, default=28)
+    ap.add_argument("--attn-hkv", type=int, default=4)
+    ap.add_argument("--attn-splits", type=int, default=0, help="0 = the library's split-KV choice")
     ap.add_argument("--e2e-batch", type=int, default=0)
     ap.add_argument("--fed-bucket", type=int, default=1,
                     help="cached dKV steps run at the fed width rounded up to this multiple (1 = exact, as the reference)")
