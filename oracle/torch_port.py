@@ -98,24 +98,26 @@ def rope(x_bhsd, cos, sin):
 
 
 def dkv_full_step_forward(layers, embed, norm_w, lm_head, ids, prefix_k, prefix_v, past_len, geo):
-    """One full dKV diffusion step of the reference on CPU (forward_dkv with
+    """One full dKV diffusion step of the reference (forward_dkv with
     is_full_step=True, modeling.py:1625-1662, through Fast_dLLM_QwenDecoderLayer
     and Fast_dLLM_QwenAttention.forward with dkv_store, modeling.py:327-415):
     embed -> per layer [RMSNorm, q/k/v, RoPE, cat(prefix, block), repeat_kv +
     SDPA under eval_mask, o_proj, residual, RMSNorm, SwiGLU MLP, residual] ->
     norm -> lm_head.  `layers` holds per-layer dicts of torch weights
     (wq, bq, wk, bk, wv, bv, wo, ln1, ln2, wg, wu, wd); prefix_k/v are
-    per-layer BHSD [B, Hkv, P, D]."""
+    per-layer BHSD [B, Hkv, P, D].  Runs on the device of `ids` (CPU for the
+    timed baseline, the GPU for the agreement test at full geometry)."""
     B, T = ids.shape
     D, Hq, Hkv = geo["head_dim"], geo["heads"], geo["kv_heads"]
+    dev = ids.device
     h = F.embedding(ids, embed)
-    pos = torch.arange(past_len, past_len + T, dtype=torch.float32)
-    inv = 1.0 / (geo["rope_theta"] ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))
+    pos = torch.arange(past_len, past_len + T, dtype=torch.float32, device=dev)
+    inv = 1.0 / (geo["rope_theta"] ** (torch.arange(0, D, 2, dtype=torch.int64, device=dev).float() / D))
     f = pos[:, None] * inv[None, :]
     emb = torch.cat((f, f), dim=-1)
     cos, sin = emb.cos().to(h.dtype)[None], emb.sin().to(h.dtype)[None]
-    qi = torch.arange(T)[:, None] + past_len
-    kj = torch.arange(T + prefix_k[0].shape[2])[None, :]
+    qi = torch.arange(T, device=dev)[:, None] + past_len
+    kj = torch.arange(T + prefix_k[0].shape[2], device=dev)[None, :]
     mask = (qi // 32) >= (kj // 32)
     for l, w in enumerate(layers):
         res = h
