@@ -23,7 +23,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FV2_REFERENCE", "/root/reference"))
+if len(sys.argv) < 2 and "FV2_REFERENCE" not in os.environ:
+    raise SystemExit("usage: python %s <path to the reference checkout> (or set FV2_REFERENCE)" % sys.argv[0])
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ["FV2_REFERENCE"])
 MODELING = REF / "models/models--Efficient-Large-Model--Fast_dLLM_v2_7B/snapshots/0661abf5f9f0ee338970d091052a26c8efa51974/modeling.py"
 
 
