@@ -67,8 +67,6 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
   const int nvec = a.H / EPV;
-  if (a.w)
-    for (int i = threadIdx.x; i < nvec; i += kNormThreads) w_s[i] = *reinterpret_cast<const uint4*>(a.w + i * 16);
   bool live = row < a.B * a.T;
   int b = 0, t = 0;
   int64_t src_t = 0;
@@ -82,7 +80,6 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
     }
   }
   uint4 v[VPL];
-  float acc = 0.f;
   if (live) {
     const char* xr = a.x + b * a.x_sb + src_t * a.x_ss;
 #pragma unroll
@@ -90,6 +87,14 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __gr
       const int vi = lane + 32 * k;
       if (vi < nvec) v[k] = ld_stream16(xr + vi * 16);
     }
+  }
+  // Weight staging (every thread of the CTA) is issued only after the row
+  // loads, so its L2 latency overlaps them instead of preceding the index
+  // load.
+  if (a.w)
+    for (int i = threadIdx.x; i < nvec; i += kNormThreads) w_s[i] = *reinterpret_cast<const uint4*>(a.w + i * 16);
+  float acc = 0.f;
+  if (live) {
     if (a.res) {
       // Residual connection (decoder layer `residual + hidden_states`): one
       // rounding to the storage dtype, then the norm of the rounded sum.
