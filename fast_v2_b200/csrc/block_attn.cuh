@@ -7,7 +7,9 @@
 // R = G*qc <= 256 rows (224 for the 7B geometry: 7 heads x 32 queries),
 // processed as one or two 128-row MMA tiles against the same K/V tiles -- the
 // GQA expansion never touches memory.  Keys stream in tiles of 128 through a
-// 2-stage TMA pipeline (64 KB of K+V per stage).
+// 2-stage TMA pipeline (64 KB of K+V per stage); each tile is also
+// prefetched into L2 one tile ahead of its shared-memory load, and a stage
+// is released as soon as the last row tile's P * V of that tile completes.
 //
 // Warp roles (320 threads):
 //   warp 0      TMA producer (Q once, then K/V tiles)
