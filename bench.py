@@ -207,13 +207,14 @@ def wl_gather_norm(args, rank, world, kt: KernelTimer):
     w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda()
     outs = [(torch.empty(B, T, H, dtype=torch.bfloat16, device="cuda"),
              torch.empty(B, T, H, dtype=torch.bfloat16, device="cuda")) for _ in range(nbuf)]
-    alg_bytes = B * T * H * 2 * 3 + B * T * 8 + H * 2  # read rows, write gathered + normed, idx, w
+    pair = not args.norm_only
+    alg_bytes = B * T * H * 2 * (3 if pair else 2) + B * T * 8 + H * 2  # read rows, write (gathered +) normed, idx, w
     state = {"i": 0}
 
     def step():
         i = state["i"] % nbuf
         state["i"] += 1
-        torch.ops.fdl.gather_rmsnorm(xs[i], idx, w, 1e-6, outs[i][0], outs[i][1])
+        torch.ops.fdl.gather_rmsnorm(xs[i], idx, w, 1e-6, outs[i][0] if pair else None, outs[i][1])
 
     # end-to-end through the public API with host buffers
     from fast_v2_b200.cuda_bench.fused_sparse_extension import fused_gather_input_rmsnorm_pair
@@ -257,6 +258,7 @@ def wl_gather_norm(args, rank, world, kt: KernelTimer):
         e2e_bytes=e2e_bytes,
         roofline=dict(bound="hbm", per_launch=alg_bytes, kernel="gather_rmsnorm_kernel"), launches_per_step=1,
         config={"workload": "gather_norm", "x": [B, S, H], "rows_per_batch": T, "dtype": "bf16",
+                "outputs": "gathered + normed (pair API)" if pair else "normed only",
                 "l2": f"inputs rotate over {nbuf} buffer sets ({nbuf * B * S * H * 2 / 2**20:.0f} MiB > L2)"},
         dtype="bf16", cpu_sample=cpu_sample)
 
@@ -265,7 +267,7 @@ def wl_kv_path(args, rank, world, kt: KernelTimer):
     from fast_v2_b200 import ensure_ops
 
     ensure_ops()
-    L, B, S, Hkv, D, rep, n = 28, 16, 4096, 4, 128, 7, 32
+    L, B, S, Hkv, D, rep, n = 28, 16, 4096, 4, 128, args.kv_rep, 32
     g = gen(2000 + rank)
     lens = torch.randint(256, 2049, (B,), generator=g, dtype=torch.int32)
     kc = [torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
@@ -581,6 +583,8 @@ def main():
     ap.add_argument("--attn-hkv", type=int, default=4)
     ap.add_argument("--attn-splits", type=int, default=0, help="0 = the library's split-KV choice")
     ap.add_argument("--e2e-batch", type=int, default=0)
+    ap.add_argument("--kv-rep", type=int, default=7, help="kv_path: GQA expansion factor of the gather (1 = none)")
+    ap.add_argument("--norm-only", action="store_true", help="gather_norm: write only the normed rows")
     ap.add_argument("--fed-bucket", type=int, default=1,
                     help="cached dKV steps run at the fed width rounded up to this multiple (1 = exact, as the reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
