@@ -414,7 +414,8 @@ def _e2e(args, rank, world, kt, geo_name):
     meta = dict(
         metric=f"generated tokens/s ({geo_name.upper()} geometry, bs{B}/GPU, block-diffusion decode)",
         unit="tokens/s", dtype="bf16",
-        config={"workload": f"e2e_{geo_name}", "model": f"Qwen2.5-{geo_name.upper()} geometry, random init",
+        config={"workload": "e2e_7b" if geo_name == "7b" else "e2e_1_5b",
+                "model": f"Qwen2.5-{geo_name.upper()} geometry, random init",
                 "params": param_count(geo), "batch_per_gpu": B, "prompt": P, "gen": G, "block": 32, "sub_block": 8,
                 "threshold": 0.9, "cache": cache_desc, "step": "one 32-token block (diffusion steps + commit)",
                 "weights": "random normal(0, 0.02); lm_head row of the mask token zeroed",
