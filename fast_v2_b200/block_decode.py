@@ -350,6 +350,8 @@ class BlockDiffusionDecoder:
         self.seed = torch.zeros(B, block, H, dtype=model.dtype, device=dev)
         self.finished = torch.zeros(B, dtype=torch.bool, device=dev)
         self.sub_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
+        self.status = torch.zeros(2, dtype=torch.long, device=dev)
+        self.status_h = torch.zeros(2, dtype=torch.long).pin_memory() if dev.type == "cuda" else torch.zeros(2, dtype=torch.long)
         self.src_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
         self._subs = [torch.arange(s, s + sub_block, device=dev) for s in range(0, block, sub_block)]
         self._srcs = [torch.clamp(t - 1, min=0) for t in self._subs]
@@ -379,6 +381,11 @@ class BlockDiffusionDecoder:
         self.finished |= ((x1 == self.stop_id) & unmask).any(dim=1)
         self.prv.copy_(self.cur)
         self.cur.copy_(self.x != self.mask_id)
+        # Loop control for the host, computed in the step itself (inside its
+        # CUDA graph): [any mask left in the current sub-block, fed width of
+        # the next cached step = max over sequences of the not-frozen count].
+        self.status[0] = (self.x.index_select(1, self.sub_idx) == self.mask_id).any()
+        self.status[1] = (~self.prv).sum(1).max()
 
     def _full_step(self):
         h = self.st.forward_block(self.x, self.pos, prefix=self.prefix)
@@ -399,7 +406,7 @@ class BlockDiffusionDecoder:
         touches is restored afterwards (the block buffers it rewrites are
         rewritten by the first full step of every block anyway)."""
         fn = self._step_fn(key)
-        bufs = (self.x, self.prv, self.cur, self.seed, self.finished)
+        bufs = (self.x, self.prv, self.cur, self.seed, self.finished, self.status)
         snap = [t.clone() for t in bufs]
         n0 = _lib.launches
         s = torch.cuda.Stream()
@@ -467,7 +474,9 @@ class BlockDiffusionDecoder:
             self.sub_idx.copy_(self._subs[sb])
             self.src_idx.copy_(self._srcs[sb])
             s, e = sb * self.sub, (sb + 1) * self.sub
-            while bool((self.x[:, s:e] == self.mask_id).any()):
+            more = bool((self.x[:, s:e] == self.mask_id).any())
+            fed_n = int((~self.prv).sum(1).max().item()) if more else 0
+            while more:
                 # Every step unmasks at least one position unless the model
                 # predicts the mask token itself (then the reference's loop
                 # never ends); fail loudly instead of spinning.
@@ -476,10 +485,13 @@ class BlockDiffusionDecoder:
                 if step_in_block <= 1 or step_in_block % self.refresh == 0:
                     self._run("full")
                 else:
-                    fed_n = int((~self.prv).sum(1).max().item())
                     self._run(min(blk, max(1, -(-fed_n // self.fed_bucket) * self.fed_bucket)))
                 n_fwd += 1
                 step_in_block += 1
+                # One device-to-host read per step: the step's own status.
+                self.status_h.copy_(self.status, non_blocking=True)
+                torch.cuda.current_stream(self.status.device).synchronize()
+                more, fed_n = bool(self.status_h[0]), int(self.status_h[1])
         x = self.x.clone()
         hl = st.forward_commit(x, self.pos)
         n_fwd += 1
