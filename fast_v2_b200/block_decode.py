@@ -351,6 +351,8 @@ class BlockDiffusionDecoder:
         self.finished = torch.zeros(B, dtype=torch.bool, device=dev)
         self.sub_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
         self.status = torch.zeros(2, dtype=torch.long, device=dev)
+        self.bridge_buf = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self.nxt = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.status_h = torch.zeros(2, dtype=torch.long).pin_memory() if dev.type == "cuda" else torch.zeros(2, dtype=torch.long)
         self.src_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
         self._subs = [torch.arange(s, s + sub_block, device=dev) for s in range(0, block, sub_block)]
@@ -397,7 +399,31 @@ class BlockDiffusionDecoder:
         h = self.st.forward_block(self.x, self.pos, fed=fed, seed_hidden=self.seed, prefix=self.prefix)
         self._sample(h)
 
+    def _begin_step(self):
+        """Block set-up: [bridge, masks...] tokens, sparse prefix selection,
+        positions, fresh dKV transfer masks."""
+        st = self.st
+        self.x.fill_(self.mask_id)
+        self.x[:, :1] = self.bridge_buf
+        self.x.masked_fill_(self.finished[:, None], self.pad_id)
+        if self.prefix == "sparse":
+            st.select_sparse_prefix()
+        self.pos.copy_(st.lens.to(torch.long)[:, None] + self.ar[None, :])
+        self.prv.zero_()
+        self.cur.zero_()
+
+    def _commit_step(self):
+        """Commit the decoded block to the KV cache; next bridge token."""
+        hl = self.st.forward_commit(self.x, self.pos)
+        nxt = self.m.logits_rows(hl).argmax(-1, keepdim=True)
+        nxt.masked_fill_(self.finished[:, None], self.pad_id)
+        self.nxt.copy_(nxt)
+
     def _step_fn(self, key):
+        if key == "begin":
+            return self._begin_step
+        if key == "commit":
+            return self._commit_step
         return self._full_step if key == "full" else (lambda: self._cached_step(key))
 
     def _capture(self, key):
@@ -406,7 +432,7 @@ class BlockDiffusionDecoder:
         touches is restored afterwards (the block buffers it rewrites are
         rewritten by the first full step of every block anyway)."""
         fn = self._step_fn(key)
-        bufs = (self.x, self.prv, self.cur, self.seed, self.finished, self.status)
+        bufs = (self.x, self.prv, self.cur, self.seed, self.finished, self.status, self.pos, self.st.lens, self.nxt)
         snap = [t.clone() for t in bufs]
         n0 = _lib.launches
         s = torch.cuda.Stream()
@@ -433,7 +459,7 @@ class BlockDiffusionDecoder:
         """Capture every step variant up front (full step and cached widths)."""
         if not self.use_graphs:
             return
-        for key in ["full"] + list(range(self.fed_bucket, self.block + 1, self.fed_bucket)):
+        for key in ["begin", "full", "commit"] + list(range(self.fed_bucket, self.block + 1, self.fed_bucket)):
             if key not in self._graphs:
                 self._capture(key)
         torch.cuda.synchronize()
@@ -459,15 +485,9 @@ class BlockDiffusionDecoder:
     def decode_block(self, bridge: torch.Tensor, stats: dict | None = None):
         """Decode one block: [bridge token, 31 masks] -> 32 tokens; commit;
         returns (block tokens [B, 32], next bridge [B, 1])."""
-        m, st, blk = self.m, self.st, self.block
-        self.x.fill_(self.mask_id)
-        self.x[:, :1] = bridge
-        self.x.masked_fill_(self.finished[:, None], self.pad_id)
-        if self.prefix == "sparse":
-            st.select_sparse_prefix()
-        self.pos.copy_(st.lens.to(torch.long)[:, None] + self.ar[None, :])
-        self.prv.zero_()
-        self.cur.zero_()
+        blk = self.block
+        self.bridge_buf.copy_(bridge)
+        self._run("begin")
         step_in_block = 0
         n_fwd = 0
         for sb in range(blk // self.sub):
@@ -493,10 +513,9 @@ class BlockDiffusionDecoder:
                 torch.cuda.current_stream(self.status.device).synchronize()
                 more, fed_n = bool(self.status_h[0]), int(self.status_h[1])
         x = self.x.clone()
-        hl = st.forward_commit(x, self.pos)
+        self._run("commit")
         n_fwd += 1
-        nxt = m.logits_rows(hl).argmax(-1, keepdim=True)
-        nxt[self.finished] = self.pad_id
+        nxt = self.nxt.clone()
         if stats is not None:
             stats["forwards"] = stats.get("forwards", 0) + n_fwd
             stats["blocks"] = stats.get("blocks", 0) + 1
