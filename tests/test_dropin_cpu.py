@@ -1,0 +1,62 @@
+"""Host-side contracts of the drop-in boundary, checked without a GPU:
+reference fallbacks that must stay (None for non-CUDA input), loud failure
+instead of a silent CPU path, and C-ABI argument checks that return before
+any device work."""
+import ctypes
+
+import pytest
+import torch
+
+from fast_v2_b200 import _lib
+from fast_v2_b200.cuda_bench.fused_sparse_extension import fused_gather_input_rmsnorm_pair
+from fast_v2_b200.utils.static_kv_cache import StaticKVCache
+
+FDL_OK, FDL_E_NULL, FDL_E_SHAPE, FDL_E_UNSUPPORTED = 0, 1, 2, 6
+
+
+class _Norm(torch.nn.Module):
+    def __init__(self, h):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.ones(h, dtype=torch.bfloat16), requires_grad=False)
+        self.variance_epsilon = 1e-6
+
+
+def test_fused_pair_returns_none_for_cpu_input_like_the_reference():
+    x = torch.randn(2, 16, 64).to(torch.bfloat16)
+    idx = torch.tensor([[0, 3], [5, 9]])
+    assert fused_gather_input_rmsnorm_pair(x, idx, _Norm(64)) is None
+
+
+def test_cpu_cache_fails_loudly_instead_of_falling_back():
+    cache = StaticKVCache(2, 64, 1, 4, 128, torch.bfloat16, torch.device("cpu"))
+    k = torch.zeros(2, 32, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises((NotImplementedError, RuntimeError)):
+        cache.write_sparse(k, k, 0, torch.zeros(2, 32, dtype=torch.long))
+
+
+def test_c_abi_argument_checks_return_before_device_work():
+    lib = _lib.abi()
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.fdl_gather_rmsnorm.argtypes = [vp, vp, i64, vp, ctypes.c_float, vp, vp, i32, i32, i32, i32, i32, i64, i64,
+                                       i64, i64, vp]
+    lib.fdl_gather_rmsnorm.restype = i32
+    fake = ctypes.c_void_p(0x1000)
+    # zero rows: nothing to do, pointers may be NULL
+    assert lib.fdl_gather_rmsnorm(None, None, 0, None, 1e-6, None, None, 1, 0, 0, 64, 0, 0, 0, 0, 0, None) == FDL_OK
+    # rows to do but no input
+    assert lib.fdl_gather_rmsnorm(None, None, 0, None, 1e-6, None, fake, 1, 4, 4, 64, 0, 0, 0, 0, 0,
+                                  None) == FDL_E_NULL
+    # identity gather asking for more rows than the sequence has
+    assert lib.fdl_gather_rmsnorm(fake, None, 0, None, 1e-6, None, fake, 1, 4, 8, 64, 0, 0, 0, 0, 0,
+                                  None) == FDL_E_SHAPE
+    lib.fdl_swiglu.argtypes = [vp, i64, vp, i64, i64, i32, vp]
+    lib.fdl_swiglu.restype = i32
+    assert lib.fdl_swiglu(fake, 16, fake, 8, 4, 12, None) == FDL_E_SHAPE  # F not a multiple of 8
+    assert lib.fdl_swiglu(None, 16, None, 8, 0, 8, None) == FDL_OK
+    lib.fdl_block_attn.argtypes = [vp, vp, vp, vp, i32, vp, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32,
+                                   ctypes.c_float] + [i64] * 12 + [i32, vp, i64, vp]
+    lib.fdl_block_attn.restype = i32
+    args = [fake, fake, fake, fake, 64, None, None, 0, None, 0, fake, 1, 32, 28, 4]
+    strides = [0] * 12
+    assert lib.fdl_block_attn(*args, 64, 0.125, *strides, 0, None, 0, None) == FDL_E_UNSUPPORTED  # head_dim 64
+    assert lib.fdl_block_attn(*args[:12], 32, 27, 4, 128, 0.125, *strides, 0, None, 0, None) == FDL_E_SHAPE
