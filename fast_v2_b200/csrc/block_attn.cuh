@@ -50,8 +50,9 @@ constexpr int kBlockN = 128;
 constexpr int kStages = 2;
 constexpr int kHeadDim = 128;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;    // + m * 128
+constexpr uint32_t kTmemS = 0;    // + m * 128 (one row tile: + buffer * 128)
 constexpr uint32_t kTmemO = 256;  // + m * 128
+constexpr uint32_t kTmemP1 = 384; // P of the single-row-tile pipeline (64 columns)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 #ifndef FDL_ATTN_PREFETCH
 #define FDL_ATTN_PREFETCH 1
@@ -91,6 +92,7 @@ struct AttnBarriers {
   uint64_t s_full[2];   // S_m(j) complete (and with it P_m(j-1) * V_(j-1))
   uint64_t p_full[2];   // P_m(j) written to TMEM (4 warp arrivals)
   uint64_t pv_done[2];  // P_m(j) * V_j complete
+  uint64_t s_free[2];   // single row tile: S buffer read by the softmax (4 warp arrivals)
   uint64_t fin;
   uint32_t tmem_base;
   int abort;
@@ -165,6 +167,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       ptx::mbar_init(&bars->s_full[m], 1);
       ptx::mbar_init(&bars->p_full[m], 4);
       ptx::mbar_init(&bars->pv_done[m], 1);
+      ptx::mbar_init(&bars->s_free[m], 4);
     }
     ptx::mbar_init(&bars->fin, 1);
     bars->abort = 0;
@@ -293,7 +296,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         }
         issued_any = true;
       }
-      for (int j = 0; ok && j < T; ++j) {
+      if (p.n_mt == 1) {
+        // One row tile (R <= 128: sub-block rows, small GQA groups): S is
+        // double-buffered in the TMEM the second tile would use and P has its
+        // own columns, so S(j+1) is computed while the softmax works on S(j)
+        // instead of after P(j) * V_j.
+        auto issue_s1 = [&](int buf, int st) {
+          const uint32_t d = tmem + kTmemS + buf * kBlockN;
+          const uint64_t kb = k_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            ptx::mma_bf16_ss(d, q_desc + ((kk >> 2) * kQHalf + (kk & 3) * 32) / 16,
+                             kb + ((kk >> 2) * kKVHalf + (kk & 3) * 32) / 16, idesc_s, kk > 0);
+        };
+        auto issue_pv1 = [&](int st, bool acc) {
+          const uint64_t vb = v_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 16; ++kk)
+            ptx::mma_bf16_ts(tmem + kTmemO, tmem + kTmemP1 + kk * 8, vb + (kk * 16 * 128) / 16, idesc_o,
+                             (acc || kk > 0) ? 1u : 0u);
+        };
+        for (int j = 0; ok && j < T; ++j) {
+          const int st = j % kStages;
+          if (j + 1 < T) {
+            ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort,
+                                kWaitTimeoutNs, 4);
+            // S(j+1) reuses the buffer of S(j-1): the softmax must have read it.
+            if (ok && j >= 1)
+              ok = ptx::mbar_wait(&bars->s_free[(j + 1) & 1], ((j - 1) >> 1) & 1, abort, kWaitTimeoutNs, 5);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            issue_s1((j + 1) & 1, (j + 1) % kStages);
+            ptx::mma_commit(&bars->s_full[(j + 1) & 1]);
+          }
+          ok = ptx::mbar_wait(&bars->p_full[0], j & 1, abort, kWaitTimeoutNs, 6);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          issue_pv1(st, j > 0);
+          ptx::mma_commit(&bars->pv_done[0]);
+          if (j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
+        }
+      }
+      for (int j = 0; ok && p.n_mt > 1 && j < T; ++j) {
         const int st = j % kStages;
         const bool nxt = j + 1 < T;
         for (int m = 0; ok && m < p.n_mt; ++m) {
@@ -348,14 +392,137 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     const uint32_t t_o = tmem + lane_off + kTmemO + m * kHeadDim;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < T; ++j) {
+    if (p.n_mt == 1) {
+      // Single row tile: S(j) in buffer j & 1, P in its own columns.
+      const uint32_t t_p = tmem + lane_off + kTmemP1;
+      const uint64_t sc2 = ptx::pack2(p.scale_log2, p.scale_log2);
+      for (int j = 0; j < T; ++j) {
+        const int buf = j & 1;
+        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[buf], (j >> 1) & 1, abort, kWaitTimeoutNs, 7));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint32_t t_sb = tmem + lane_off + kTmemS + buf * kBlockN;
+        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+        const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : kBlockN;
+        const bool full = __all_sync(0xffffffffu, climit == kBlockN);
+        // Max of 64 columns [c0, c0 + 64) held in lo / hi.
+        auto half_max = [&](const float (&lo)[32], const float (&hi)[32], int c0) {
+          float mx = -INFINITY;
+          if (full) {
+            float a0 = lo[0], a1 = hi[0];
+#pragma unroll
+            for (int i = 1; i < 31; i += 2) {
+              a0 = ptx::fmax3(a0, lo[i], lo[i + 1]);
+              a1 = ptx::fmax3(a1, hi[i], hi[i + 1]);
+            }
+            mx = ptx::fmax3(a0, a1, fmaxf(lo[31], hi[31]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (c0 + i < climit) mx = fmaxf(mx, lo[i]);
+              if (c0 + 32 + i < climit) mx = fmaxf(mx, hi[i]);
+            }
+          }
+          return mx;
+        };
+        float sa[32], sb[32];
+        ptx::tmem_ld32(t_sb + 64, sa);
+        ptx::tmem_ld32(t_sb + 96, sb);
+        ptx::tmem_wait_ld();
+        float tmax = half_max(sa, sb, 64);
+        ptx::tmem_ld32(t_sb + 0, sa);
+        ptx::tmem_ld32(t_sb + 32, sb);
+        ptx::tmem_wait_ld();
+        tmax = fmaxf(tmax, half_max(sa, sb, 0));
+        tmax *= p.scale_log2;
+        const float m_new = fmaxf(m_used, tmax);
+        const bool grow = m_new > m_used + 8.f;
+        const bool rescale = grow && (m_used != -INFINITY) && j > 0;
+        const float alpha = rescale ? ptx::ex2(m_used - m_new) : 1.f;
+        if (grow) {
+          l = (m_used == -INFINITY) ? 0.f : l * alpha;
+          m_used = m_new;
+        }
+        // P and O are in use by P(j-1) * V_(j-1) until it completes.
+        if (j > 0) {
+          ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[0], (j - 1) & 1, abort, kWaitTimeoutNs, 8));
+          if (!ok) break;
+          ptx::tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            float o[32];
+            ptx::tmem_ld32(t_o + ch * 32, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            ptx::tmem_st32(t_o + ch * 32, o);
+          }
+        }
+        const float neg_m = -m_used;
+        const uint64_t nm2 = ptx::pack2(neg_m, neg_m);
+        uint64_t acc2 = ptx::pack2(0.f, 0.f);
+        float rsum = 0.f;
+        auto emit = [&](const float (&sv)[32], int c) {
+          uint32_t pk[16];
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
+              float x0, x1;
+              ptx::unpack2(x2, x0, x1);
+              const uint64_t e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
+              acc2 = ptx::add2(acc2, e2);
+              float p0, p1;
+              ptx::unpack2(e2, p0, p1);
+              const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+              pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int k0 = c * 32 + 2 * i;
+              const float p0 = (k0 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i], p.scale_log2, neg_m)) : 0.f;
+              const float p1 = (k0 + 1 < climit) ? ptx::ex2(__fmaf_rn(sv[2 * i + 1], p.scale_log2, neg_m)) : 0.f;
+              rsum += p0 + p1;
+              const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+              pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+          }
+          ptx::tmem_st16(t_p + c * 16, pk);
+        };
+        emit(sa, 0);
+        emit(sb, 1);
+        ptx::tmem_ld32(t_sb + 64, sa);
+        ptx::tmem_ld32(t_sb + 96, sb);
+        ptx::tmem_wait_ld();
+        // Every column of S(j) is in registers: its buffer may take S(j+2).
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->s_free[buf]);
+        emit(sa, 2);
+        emit(sb, 3);
+        float s0, s1;
+        ptx::unpack2(acc2, s0, s1);
+        l += rsum + (s0 + s1);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->p_full[0]);
+      }
+    }
+    for (int j = 0; p.n_mt > 1 && j < T; ++j) {
       // S_m(j) ready (and P_m(j-1) * V_(j-1) done: O_m is stable).
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], j & 1, abort, kWaitTimeoutNs, 7));
       if (!ok) break;
       ptx::tc_fence_after();
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
       // Visible keys of this tile for this row form a prefix of the tile.
-      const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : 0;
+      // Padding rows (beyond the R real rows, or past the last query) count
+      // as fully visible: their results are never stored, and this keeps
+      // whole warps of padding rows on the unpredicated path.
+      const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : kBlockN;
       // The S row is read in halves of 64 columns so no more than 64 values
       // are live: the upper half (keys 64..127) is read first for its max,
       // then the lower half, which stays in registers; after the lower
