@@ -380,6 +380,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     const int q = q0 + sq_i;
     const int head = g * p.G + (r - sq_i * p.G);
     const bool valid_row = (r < R) && (q < p.Sq);
+    // A warp whose 32 rows are all padding has nothing to compute: its P
+    // lanes feed only O rows that are never stored, so it just keeps the
+    // barrier phases (and leaves its SM sub-partition to the other warps).
+    const bool pad_warp = __all_sync(0xffffffffu, !valid_row);
     // Block-causal mask as a key-position bound: key position kp is visible
     // iff kp / mask_block <= qpos / mask_block, i.e. kp < kpos_end.
     int kpos_end = 0x7fffffff;
@@ -401,6 +405,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[buf], (j >> 1) & 1, abort, kWaitTimeoutNs, 7));
         if (!ok) break;
         ptx::tc_fence_after();
+        if (pad_warp) {
+          __syncwarp();
+          if (lane == 0) {
+            ptx::mbar_arrive(&bars->s_free[buf]);
+            ptx::mbar_arrive(&bars->p_full[0]);
+          }
+          continue;
+        }
         const uint32_t t_sb = tmem + lane_off + kTmemS + buf * kBlockN;
         const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
         const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : kBlockN;
@@ -517,6 +529,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], j & 1, abort, kWaitTimeoutNs, 7));
       if (!ok) break;
       ptx::tc_fence_after();
+      if (pad_warp) {
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->p_full[m]);
+        continue;
+      }
       const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
       // Visible keys of this tile for this row form a prefix of the tile.
       // Padding rows (beyond the R real rows, or past the last query) count
