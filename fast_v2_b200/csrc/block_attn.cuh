@@ -36,7 +36,14 @@
 // (Two issuers, one per row tile, keep the pipe fuller in isolation but slow
 // the softmax warps, which bound the kernel, by more.)
 //
-// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
+// With a single row tile (R <= 128) the second tile's TMEM holds a second S
+// buffer and P gets its own columns, so S(j+1) overlaps the softmax of S(j).
+// Padding rows (beyond R or past the last query) count as fully visible and
+// whole warps of them skip the softmax, so they never take the predicated
+// path that would make their row tile wait for them.
+//
+// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512)
+// (one row tile: S buffers [0,128) [128,256), O [256,384), P [384,448)).
 // Shared memory: Q 64 KB | K 2x32 KB | V 2x32 KB | barriers.
 #pragma once
 #include <cuda.h>
