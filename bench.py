@@ -15,6 +15,8 @@ Configs (BASELINE.json `configs`):
                 GQA-7 expansion, cache [16, 4096, 4, 128] per layer and K/V
   block_attn    block attention Q [B, 32, 28, 128] over a prefix of P keys
                 (--attn-b, --attn-p, --attn-sq select the point)
+  compact       in-place batch compaction of the 7B decode cache (28 layers
+                of K/V [64, 2304, 4, 128], every fourth slot finished)
   e2e_7b        (default) block-diffusion decode at Qwen2.5-7B geometry,
                 random init, 64 sequences/GPU, prompt 1024, dKV block cache
                 + token-sparse prefix; one step = one 32-token block
@@ -524,6 +526,44 @@ def _e2e(args, rank, world, kt, geo_name):
                 launches_per_step=None, stats=stats, cpu_sample=cpu_sample)
 
 
+def wl_compact(args, rank, world, kt: KernelTimer):
+    """In-place batch compaction of the 7B decode cache (28 layers of K and V
+    [64, 2304, 4, 128]) after every fourth slot finished: the kernel behind
+    every cache class's compact_batch, one launch for all 56 buffers."""
+    from fast_v2_b200 import ensure_ops
+
+    ensure_ops()
+    L, B, S, Hkv, D = 28, 64, 2304, 4, 128
+    dg = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    bufs = [torch.randn(B, S, Hkv, D, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(2 * L)]
+    keep = [i for i in range(B) if i % 4 != 3]
+    act = torch.tensor(keep, dtype=torch.int64, device="cuda")
+    moved = sum(1 for i, a in enumerate(keep) if a != i)
+    row_bytes = S * Hkv * D * 2
+    alg = 2 * moved * row_bytes * 2 * L  # read + write of every moved row
+
+    def step():
+        torch.ops.fdl.kv_compact(bufs, act)
+
+    def cpu_sample():
+        from oracle import kvcache_oracle as O
+
+        hb = [bufs[j].cpu().view(torch.int16).numpy() for j in range(2)]
+        t0 = time.perf_counter()
+        for h in hb:
+            O.batch_compact(h, keep)
+        dt = (time.perf_counter() - t0) / len(hb) * 2 * L
+        return alg / dt / 1e9, "2 of 56 buffers (t[active] gather), scaled to 56"
+
+    return dict(
+        metric="batch compaction throughput (algorithmic HBM GB/s)", unit="GB/s",
+        units_per_step=alg / 1e9, step=step, dominant=step, graph=True, e2e_step=None, e2e_bytes=None,
+        roofline=dict(bound="hbm", per_launch=alg, kernel="kv_compact_kernel"), launches_per_step=1,
+        config={"workload": "compact", "layers": L, "cache": [B, S, Hkv, D], "kept": len(keep), "moved_rows": moved,
+                "l2": f"working set {2 * L * B * row_bytes / 2**30:.1f} GiB > L2"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
 def wl_e2e_7b(args, rank, world, kt):
     return _e2e(args, rank, world, kt, "7b")
 
@@ -532,7 +572,7 @@ def wl_e2e_1_5b(args, rank, world, kt):
     return _e2e(args, rank, world, kt, "1.5b")
 
 
-WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn,
+WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn, "compact": wl_compact,
              "e2e_7b": wl_e2e_7b, "e2e_1_5b": wl_e2e_1_5b}
 DEFAULT_CONFIG = "e2e_7b"
 

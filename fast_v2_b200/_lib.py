@@ -22,6 +22,7 @@ EXPORTS = (
     "fdl_kv_scatter",
     "fdl_kv_gather_prefix",
     "fdl_kv_gather_rows",
+    "fdl_kv_compact",
     "fdl_sparse_prefix_workspace_bytes",
     "fdl_kv_sparse_prefix",
     "fdl_kv_sparse_prefix_noalloc",

@@ -253,6 +253,40 @@ int fdl_kv_gather_rows(const void* k_src, const void* v_src, const void* idx, in
   return launch_status();
 }
 
+int fdl_kv_compact(void* const* bufs, int n_bufs, int64_t row_bytes, int64_t batch_stride, int batch,
+                   const int64_t* active, int n_keep, fdl_stream_t stream) {
+  if (n_keep == 0 || n_bufs == 0 || row_bytes == 0) return FDL_OK;
+  if (!bufs || !active) return FDL_E_NULL;
+  if (n_bufs < 0 || n_keep < 0 || batch < 1 || batch > 65535 || n_keep > batch || n_keep > kCompactMaxRows ||
+      row_bytes < 0 || batch_stride < row_bytes)
+    return FDL_E_SHAPE;
+  uint64_t align_acc = 0;
+  for (int j = 0; j < n_bufs; ++j) {
+    if (!bufs[j]) return FDL_E_NULL;
+    align_acc |= reinterpret_cast<uintptr_t>(bufs[j]);
+  }
+  const int vec = pick_vec({static_cast<uint64_t>(row_bytes), static_cast<uint64_t>(batch_stride), align_acc});
+  if (vec < 2) return FDL_E_ALIGN;
+  const uint64_t vpr = static_cast<uint64_t>(row_bytes) / vec;
+  if (vpr >= (1ull << 31)) return FDL_E_SHAPE;
+  CompactArgs a{};
+  a.active = active;
+  a.n_keep = n_keep;
+  a.batch = batch;
+  a.stride = batch_stride;
+  a.vpr = static_cast<uint32_t>(vpr);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int j0 = 0; j0 < n_bufs; j0 += kCompactMaxBufs) {
+    const int nb = std::min(kCompactMaxBufs, n_bufs - j0);
+    for (int j = 0; j < nb; ++j) a.buf[j] = static_cast<char*>(bufs[j0 + j]);
+    const dim3 grid(static_cast<uint32_t>((vpr + kCopyThreads - 1) / kCopyThreads), nb);
+    launch_vec<CompactL>(vec, grid, a, s);
+    const int rc = launch_status();
+    if (rc != FDL_OK) return rc;
+  }
+  return FDL_OK;
+}
+
 int64_t fdl_sparse_prefix_workspace_bytes(int batch, int cap) {
   const int64_t b = static_cast<int64_t>(batch) * cap * 4;
   return (b + 255) / 256 * 256;

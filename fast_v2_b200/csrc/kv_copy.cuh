@@ -226,6 +226,63 @@ __global__ void __launch_bounds__(kCopyThreads) kv_gather_rows_kernel(const __gr
     if (ooff[u] >= 0) st_vec<VEC>(out + ooff[u], buf[u]);
 }
 
+// ------------------------------------------------------ batch compaction --
+// In-place gather along the batch axis of up to kCompactMaxBufs buffers:
+// row i <- row active[i] for i < n_keep.  A thread owns one VEC-byte column
+// of every row of one buffer and walks the rows in increasing i, so no two
+// threads touch the same bytes, and when i <= active[i] for every i the
+// source row of step i is still unwritten (the rows written before step i
+// are all < i <= active[i]).  Every CTA checks that condition over the whole
+// list before touching memory; a list outside it moves nothing and is
+// reported as FDL_DEV_INDEX.  Rows with active[i] == i are not touched.
+constexpr int kCompactMaxBufs = 128;
+constexpr int kCompactMaxRows = 4096;
+constexpr int kCompactUnroll = 8;
+
+struct CompactArgs {
+  char* buf[kCompactMaxBufs];
+  const int64_t* active;
+  int n_keep, batch;
+  int64_t stride;  // bytes between consecutive batch rows
+  uint32_t vpr;    // VEC-byte vectors per row
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(kCopyThreads) kv_compact_kernel(const __grid_constant__ CompactArgs a) {
+  using V = typename VecT<VEC>::T;
+  __shared__ int s_act[kCompactMaxRows];
+  bool ok = true;
+  long long bad = 0;
+  for (int i = threadIdx.x; i < a.n_keep; i += kCopyThreads) {
+    const int64_t s = a.active[i];
+    if (s < i || s >= a.batch) {
+      ok = false;
+      bad = s;
+    }
+    s_act[i] = static_cast<int>(s);
+  }
+  if (!__syncthreads_and(ok)) {
+    if (!ok && blockIdx.x == 0 && blockIdx.y == 0) report(FDL_DEV_INDEX, bad);
+    return;
+  }
+  const uint32_t v = blockIdx.x * kCopyThreads + threadIdx.x;
+  if (v >= a.vpr) return;
+  char* col = a.buf[blockIdx.y] + static_cast<int64_t>(v) * VEC;
+  for (int i0 = 0; i0 < a.n_keep; i0 += kCompactUnroll) {
+    V buf[kCompactUnroll];
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const int i = i0 + u;
+      if (i < a.n_keep && s_act[i] != i) buf[u] = ld_vec<VEC>(col + s_act[i] * a.stride);
+    }
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const int i = i0 + u;
+      if (i < a.n_keep && s_act[i] != i) st_vec<VEC>(col + i * a.stride, buf[u]);
+    }
+  }
+}
+
 template <template <int> class K, class Args>
 inline void launch_vec(int vec, dim3 grid, const Args& a, cudaStream_t s) {
   switch (vec) {
@@ -247,6 +304,9 @@ template <int VEC> struct GatherPrefixL {
 };
 template <int VEC> struct GatherRowsL {
   static void launch(dim3 g, const GatherRowsArgs& a, cudaStream_t s) { kv_gather_rows_kernel<VEC><<<g, kCopyThreads, 0, s>>>(a); }
+};
+template <int VEC> struct CompactL {
+  static void launch(dim3 g, const CompactArgs& a, cudaStream_t s) { kv_compact_kernel<VEC><<<g, kCopyThreads, 0, s>>>(a); }
 };
 
 inline uint32_t copy_blocks(uint64_t total) {

@@ -10,6 +10,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <vector>
+
 #include "../../include/fdl_kvcache.h"
 
 namespace {
@@ -229,6 +231,45 @@ void kv_gather_rows(const Tensor& k_src, const std::optional<Tensor>& v_src, con
                               static_cast<int>(s.S), static_cast<int>(s.H), static_cast<int>(s.D), elem_bytes(k_src),
                               s.sb, s.ss, s.sh, o.sb, o.ss, o.sh, cur_stream()),
            "kv_gather_rows");
+}
+
+// True when every batch row (dims 1..) of t is one contiguous run.
+bool rows_contiguous(const Tensor& t) {
+  int64_t expect = 1;
+  for (int64_t d = t.dim() - 1; d >= 1; --d) {
+    if (t.size(d) != 1 && t.stride(d) != expect) return false;
+    expect *= t.size(d);
+  }
+  return true;
+}
+
+// In-place batch compaction of buffers that share the batch size, the row
+// size in bytes and the batch stride in bytes: row i <- row active[i].
+void kv_compact(at::TensorList bufs, const Tensor& active) {
+  TORCH_CHECK(active.is_cuda() && active.scalar_type() == at::kLong && active.dim() == 1 && active.is_contiguous(),
+              "fdl.kv_compact: active must be a contiguous CUDA int64 [n] tensor");
+  if (bufs.empty() || active.numel() == 0) return;
+  const Tensor& b0 = bufs[0];
+  TORCH_CHECK(b0.dim() >= 1, "fdl.kv_compact: buffers need a batch dimension");
+  const int64_t B = b0.size(0);
+  TORCH_CHECK(active.numel() <= B, "fdl.kv_compact: ", active.numel(), " active rows for a batch of ", B);
+  const int64_t row_bytes = (b0.numel() / B) * static_cast<int64_t>(b0.element_size());
+  const int64_t stride_bytes = b0.stride(0) * static_cast<int64_t>(b0.element_size());
+  std::vector<void*> ptrs;
+  ptrs.reserve(bufs.size());
+  for (const Tensor& t : bufs) {
+    TORCH_CHECK(t.is_cuda() && t.device() == active.device(), "fdl.kv_compact: buffers must be on ", active.device());
+    TORCH_CHECK(t.dim() >= 1 && t.size(0) == B, "fdl.kv_compact: all buffers must share the batch size ", B);
+    TORCH_CHECK((t.numel() / B) * static_cast<int64_t>(t.element_size()) == row_bytes &&
+                    t.stride(0) * static_cast<int64_t>(t.element_size()) == stride_bytes,
+                "fdl.kv_compact: all buffers must share the row size and batch stride in bytes");
+    TORCH_CHECK(rows_contiguous(t), "fdl.kv_compact: each batch row must be contiguous");
+    ptrs.push_back(t.data_ptr());
+  }
+  c10::cuda::CUDAGuard guard(active.device());
+  check_rc(fdl_kv_compact(ptrs.data(), static_cast<int>(ptrs.size()), row_bytes, stride_bytes, static_cast<int>(B),
+                          active.data_ptr<int64_t>(), static_cast<int>(active.numel()), cur_stream()),
+           "kv_compact");
 }
 
 void kv_sparse_prefix(const Tensor& k, const Tensor& v, const Tensor& lens, int64_t keep_num, int64_t keep_den,
@@ -466,6 +507,7 @@ TORCH_LIBRARY(fdl, m) {
         "int rep, Tensor(a!) k_out, Tensor(b!) v_out, Tensor? cu_seqlens, int seq_dim_in, int seq_dim_out) -> ()");
   m.def("kv_gather_rows(Tensor k_src, Tensor? v_src, Tensor idx, Tensor? count, Tensor(a!) k_out, "
         "Tensor(b!)? v_out, int seq_dim) -> ()");
+  m.def("kv_compact(Tensor(a!)[] bufs, Tensor active) -> ()");
   m.def("kv_sparse_prefix(Tensor k, Tensor v, Tensor lens, int keep_num, int keep_den, Tensor(a!) sel, "
         "Tensor(b!) out_len, Tensor(c!)? k_out, Tensor(d!)? v_out, Tensor(e!) workspace) -> ()");
   m.def("gather_rmsnorm(Tensor x, Tensor? idx, Tensor? weight, float eps, Tensor(a!)? gathered, "
@@ -485,6 +527,7 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("kv_scatter", &kv_scatter);
   m.impl("kv_gather_prefix", &kv_gather_prefix);
   m.impl("kv_gather_rows", &kv_gather_rows);
+  m.impl("kv_compact", &kv_compact);
   m.impl("kv_sparse_prefix", &kv_sparse_prefix);
   m.impl("gather_rmsnorm", &gather_rmsnorm);
   m.impl("block_attn", &block_attn);
@@ -503,6 +546,7 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
             int64_t, const Tensor&, const Tensor&, const std::optional<Tensor>&, int64_t, int64_t) {});
   m.impl("kv_gather_rows", [](const Tensor&, const std::optional<Tensor>&, const Tensor&,
                               const std::optional<Tensor>&, const Tensor&, const std::optional<Tensor>&, int64_t) {});
+  m.impl("kv_compact", [](at::TensorList, const Tensor&) {});
   m.impl("kv_sparse_prefix",
          [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
             const std::optional<Tensor>&, const std::optional<Tensor>&, const Tensor&) {});

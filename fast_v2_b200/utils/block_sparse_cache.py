@@ -11,6 +11,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
+from .compaction import active_rows, compact_rows
 
 
 class BlockSparseCache:
@@ -63,8 +64,14 @@ class BlockSparseCache:
         pass
 
     def compact_batch(self, active_indices: torch.Tensor):
-        self.layer_input = self.layer_input[:, active_indices].contiguous()
-        self.attn_output = self.attn_output[:, active_indices].contiguous()
-        self.mlp_input = self.mlp_input[:, active_indices].contiguous()
-        self.mlp_output = self.mlp_output[:, active_indices].contiguous()
-        self.batch_size = active_indices.numel()
+        """Drop finished batch slots (utils/block_sparse_cache.py:141-147) in
+        place: the four [L, B, block, hidden] buffers keep their storage and
+        become [L, n, block, hidden] views (each layer's slice stays
+        contiguous).  active_indices[i] must lie in [i, batch_size) -- any
+        ascending list of distinct slots."""
+        act = active_rows(active_indices, self.batch_size, self.device)
+        n = act.numel()
+        bufs = (self.layer_input, self.attn_output, self.mlp_input, self.mlp_output)
+        compact_rows([t.select(0, l) for t in bufs for l in range(self.num_layers)], act)
+        self.layer_input, self.attn_output, self.mlp_input, self.mlp_output = (t[:, :n] for t in bufs)
+        self.batch_size = n

@@ -11,6 +11,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
+from .compaction import active_rows, compact_rows
 
 
 class DynamicBlockKV:
@@ -47,8 +48,15 @@ class DynamicBlockKV:
         pass
 
     def compact_batch(self, active_indices):
+        """Drop finished batch slots (utils/dynamic_block_kv.py:52-56) in
+        place: every per-layer buffer keeps its storage and becomes a prefix
+        view.  active_indices[i] must lie in [i, batch_size) -- any ascending
+        list of distinct slots."""
+        act = active_rows(active_indices, self.batch_size, self.device)
+        n = act.numel()
+        compact_rows(list(self.k.values()) + list(self.v.values()), act)
         for L in self.k:
-            self.k[L] = self.k[L][active_indices].contiguous()
-            self.v[L] = self.v[L][active_indices].contiguous()
-        self.batch_size = active_indices.numel()
-        self._zero_start = torch.zeros(self.batch_size, dtype=torch.int32, device=self.device)
+            self.k[L] = self.k[L][:n]
+            self.v[L] = self.v[L][:n]
+        self.batch_size = n
+        self._zero_start = self._zero_start[:n]

@@ -28,6 +28,7 @@ from typing import Optional
 import torch
 
 from .. import _lib
+from .compaction import active_rows, compact_rows, regrow
 
 
 def _mark(t: torch.Tensor) -> None:
@@ -212,37 +213,45 @@ class StaticKVCache:
         self.kv_write_start.fill_(0)
 
     def restore_full_batch(self):
+        """Back to max_batch_size after compact_batch (utils/static_kv_cache.py:
+        319-348): the prefix views grow back over their own storage, zeroed as
+        the reference's fresh buffers are, so data pointers do not change."""
         if self.batch_size == self.max_batch_size:
             return
         bs = self.max_batch_size
-        self.key_cache = [torch.zeros(bs, self.max_seq_len, self.num_kv_heads, self.head_dim, dtype=self.dtype,
-                                      device=self.device) for _ in range(self.num_layers)]
-        self.value_cache = [torch.zeros(bs, self.max_seq_len, self.num_kv_heads, self.head_dim, dtype=self.dtype,
-                                        device=self.device) for _ in range(self.num_layers)]
-        self.cache_seqlens = torch.zeros(bs, dtype=torch.int32, device=self.device)
-        self.scratch_seqlens = torch.zeros(bs, dtype=torch.int32, device=self.device)
-        self._attn_mask_buffer = torch.zeros(bs, 1, 1, self.max_seq_len, dtype=self.dtype, device=self.device)
-        self._commit_start = torch.zeros(bs, dtype=torch.int32, device=self.device)
-        self._scratch_start = torch.zeros(bs, dtype=torch.int32, device=self.device)
+        self.key_cache = [regrow(t, bs) for t in self.key_cache]
+        self.value_cache = [regrow(t, bs) for t in self.value_cache]
+        self.cache_seqlens = regrow(self.cache_seqlens, bs)
+        self.scratch_seqlens = regrow(self.scratch_seqlens, bs)
+        self._attn_mask_buffer = regrow(self._attn_mask_buffer, bs)
+        self._commit_start = regrow(self._commit_start, bs)
+        self._scratch_start = regrow(self._scratch_start, bs)
         self._commit_start_value = 0
         self._seq_len = 0
         self.kv_write_start.fill_(0)
         self.batch_size = bs
 
     def compact_batch(self, active_indices: torch.Tensor):
-        """Drop finished batch slots (utils/static_kv_cache.py:350-398); eager
-        only -- creates new tensors."""
-        n_active = active_indices.numel()
-        self.key_cache = [self.key_cache[i][active_indices].contiguous() for i in range(self.num_layers)]
-        self.value_cache = [self.value_cache[i][active_indices].contiguous() for i in range(self.num_layers)]
-        self.cache_seqlens = self.cache_seqlens[active_indices].contiguous()
-        self.scratch_seqlens = self.scratch_seqlens[active_indices].contiguous()
-        self._commit_start = self._commit_start[active_indices].contiguous()
-        self._scratch_start = self._scratch_start[active_indices].contiguous()
+        """Drop finished batch slots (utils/static_kv_cache.py:350-398) in
+        place: row i of every batch-indexed buffer takes row
+        active_indices[i], then each buffer becomes a prefix view of its own
+        storage, so data pointers stay valid for CUDA graphs.
+        active_indices[i] must lie in [i, batch_size) for every i -- any
+        ascending list of distinct slots, as ``nonzero()`` returns; other
+        lists raise ValueError."""
+        act = active_rows(active_indices, self.batch_size, self.device)
+        n = act.numel()
+        compact_rows(self.key_cache + self.value_cache, act)
+        compact_rows([self.cache_seqlens, self.scratch_seqlens, self._commit_start, self._scratch_start], act)
+        self.key_cache = [t[:n] for t in self.key_cache]
+        self.value_cache = [t[:n] for t in self.value_cache]
+        self.cache_seqlens = self.cache_seqlens[:n]
+        self.scratch_seqlens = self.scratch_seqlens[:n]
+        self._commit_start = self._commit_start[:n]
+        self._scratch_start = self._scratch_start[:n]
         self._write_idx_fixed = None
-        self._attn_mask_buffer = torch.zeros(n_active, 1, 1, self.max_seq_len, dtype=self.dtype, device=self.device)
-        self._kv_indices = torch.arange(self.max_seq_len, dtype=torch.int32, device=self.device)
-        self.batch_size = n_active
+        self._attn_mask_buffer = self._attn_mask_buffer[:n].zero_()
+        self.batch_size = n
 
 
 class StaticBlockCache:
@@ -293,8 +302,12 @@ class StaticBlockCache:
         self._num_initialized = 0
 
     def compact_batch(self, active_indices: torch.Tensor):
-        n_active = active_indices.numel()
-        self.key_cache = [self.key_cache[i][active_indices].contiguous() for i in range(self.num_layers)]
-        self.value_cache = [self.value_cache[i][active_indices].contiguous() for i in range(self.num_layers)]
-        self._zero_start = torch.zeros(n_active, dtype=torch.int32, device=self.device)
-        self.batch_size = n_active
+        """In place, like StaticKVCache.compact_batch (reference:
+        utils/static_kv_cache.py:473-491)."""
+        act = active_rows(active_indices, self.batch_size, self.device)
+        n = act.numel()
+        compact_rows(self.key_cache + self.value_cache, act)
+        self.key_cache = [t[:n] for t in self.key_cache]
+        self.value_cache = [t[:n] for t in self.value_cache]
+        self._zero_start = self._zero_start[:n]
+        self.batch_size = n

@@ -153,6 +153,32 @@ int fdl_kv_gather_rows(const void* k_src, const void* v_src,
                        fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * (a) In-place batch compaction (storage and addresses unchanged).
+ *
+ * For every buffer j < n_bufs and every i < n_keep, in increasing i:
+ *   bufs[j][i * batch_stride : + row_bytes] = bufs[j][active[i] * batch_stride : + row_bytes]
+ * Each buffer holds `batch` rows of row_bytes bytes, batch_stride bytes
+ * apart (batch_stride >= row_bytes).  active is a device int64 [n_keep]
+ * with i <= active[i] < batch for every i: every ascending list of distinct
+ * slots (torch.nonzero of an active mask, utils/batch_bucketing.py:135)
+ * qualifies.  The kernel checks the whole list before moving anything; a
+ * list outside that set moves nothing and is reported as FDL_DEV_INDEX
+ * (info = the offending entry).  Rows with active[i] == i are not touched;
+ * rows >= n_keep keep stale bytes.  n_keep <= 4096; any number of buffers
+ * (128 per launch); the copy is bit-exact for any element type.
+ *
+ * Replaces the batch re-indexing `t[active_indices].contiguous()` of
+ * StaticKVCache.compact_batch (utils/static_kv_cache.py:350-398),
+ * StaticBlockCache.compact_batch (utils/static_kv_cache.py:473-491),
+ * DynamicBlockKV.compact_batch (utils/dynamic_block_kv.py:52-56) and
+ * BlockSparseCache.compact_batch (utils/block_sparse_cache.py:141-147),
+ * which allocate new tensors: the caches here keep their buffers and shrink
+ * to a prefix view, so addresses baked into CUDA graphs stay valid.
+ * ---------------------------------------------------------------------- */
+int fdl_kv_compact(void* const* bufs, int n_bufs, int64_t row_bytes, int64_t batch_stride,
+                   int batch, const int64_t* active, int n_keep, fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * (b) Token-sparse prefix selection ("keep the top keep_num/keep_den of the
  * committed prefix tokens by key norm").  No reference counterpart exists;
  * the specification is:

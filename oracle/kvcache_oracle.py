@@ -134,6 +134,30 @@ def gather_rows(src, idx, seq_axis: int = 1):
     return np.stack([src[b][:, idx[b]] for b in range(B)])
 
 
+def batch_compact(buf, active, batch_axis: int = 0):
+    """``t[active_indices].contiguous()`` along the batch axis: the reference's
+    compaction of every batch-indexed cache buffer
+    (utils/static_kv_cache.py:366-379, :483-490; utils/dynamic_block_kv.py:52-56;
+    utils/block_sparse_cache.py:143-146 with the batch on axis 1)."""
+    return np.take(buf, np.asarray(active, dtype=np.int64), axis=batch_axis)
+
+
+def batch_compact_in_place(buf, active):
+    """The in-place order of the CUDA compaction, restated sequentially: for
+    i = 0, 1, ... row i takes row active[i] of the partly updated buffer.
+    Equal to ``batch_compact`` on the first len(active) rows whenever
+    i <= active[i] < batch for every i; returns False (buffer untouched)
+    for any other list, as the kernel reports it and moves nothing."""
+    active = np.asarray(active, dtype=np.int64)
+    n = active.shape[0]
+    if np.any(active < np.arange(n)) or np.any(active >= buf.shape[0]):
+        return False
+    for i in range(n):
+        if active[i] != i:
+            buf[i] = buf[active[i]]
+    return True
+
+
 def key_norm_scores(k_bits, lens):
     """Token-sparse prefix score (no reference counterpart; specification):
     score[b, t] = sqrt(sum over (h, d) of K[b, t, h, d]^2) in fp32 for t < lens[b],

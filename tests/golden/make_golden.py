@@ -213,6 +213,58 @@ def gen_index_ops(ref):
     np.savez_compressed(HERE / "index_ops.npz", **out)
 
 
+def gen_compaction(ref):
+    """compact_batch of StaticKVCache, StaticBlockCache, DynamicBlockKV and
+    BlockSparseCache (utils/static_kv_cache.py:350-398, :473-491,
+    utils/dynamic_block_kv.py:52-56, utils/block_sparse_cache.py:141-147),
+    applied twice (5 -> 3 -> 2 slots), then StaticKVCache.restore_full_batch."""
+    g = torch.Generator().manual_seed(13)
+    B, S, L, H, D, blk, hid = 5, 48, 2, 2, 64, 8, 64
+    rnd = lambda *shape: torch.randn(*shape, generator=g).to(torch.bfloat16)  # noqa: E731
+    steps = (torch.tensor([1, 2, 4]), torch.tensor([0, 2]))
+    out = {"active_0": steps[0].numpy(), "active_1": steps[1].numpy()}
+    c = ref.skv.StaticKVCache(B, S, L, H, D, torch.bfloat16, torch.device("cpu"))
+    sb = ref.skv.StaticBlockCache(B, blk, L, H, D, torch.bfloat16, torch.device("cpu"))
+    dk = ref.dbk.DynamicBlockKV(1, L + 1, B, H, blk, D, torch.bfloat16, torch.device("cpu"))
+    bs = ref.bsc.BlockSparseCache(L, B, blk, hid, torch.bfloat16, torch.device("cpu"))
+    for l in range(L):
+        c.key_cache[l].copy_(rnd(B, S, H, D))
+        c.value_cache[l].copy_(rnd(B, S, H, D))
+        sb.key_cache[l].copy_(rnd(B, blk, H, D))
+        sb.value_cache[l].copy_(rnd(B, blk, H, D))
+    for l in dk.k:
+        dk.k[l].copy_(rnd(B, H, blk, D))
+        dk.v[l].copy_(rnd(B, H, blk, D))
+    for name in ("layer_input", "attn_output", "mlp_input", "mlp_output"):
+        getattr(bs, name).copy_(rnd(L, B, blk, hid))
+    c.cache_seqlens.copy_(torch.tensor([40, 7, 33, 12, 25], dtype=torch.int32))
+    c.scratch_seqlens.copy_(torch.tensor([41, 8, 34, 13, 26], dtype=torch.int32))
+
+    def snapshot(tag):
+        for l in range(L):
+            out[f"{tag}_skv_k{l}"], out[f"{tag}_skv_v{l}"] = bits(c.key_cache[l]), bits(c.value_cache[l])
+            out[f"{tag}_sbc_k{l}"], out[f"{tag}_sbc_v{l}"] = bits(sb.key_cache[l]), bits(sb.value_cache[l])
+        for l in dk.k:
+            out[f"{tag}_dbk_k{l}"], out[f"{tag}_dbk_v{l}"] = bits(dk.k[l]), bits(dk.v[l])
+        for name in ("layer_input", "attn_output", "mlp_input", "mlp_output"):
+            out[f"{tag}_bsc_{name}"] = bits(getattr(bs, name))
+        out[f"{tag}_cache_seqlens"] = c.cache_seqlens.numpy().copy()
+        out[f"{tag}_scratch_seqlens"] = c.scratch_seqlens.numpy().copy()
+        out[f"{tag}_batch"] = np.int64(c.batch_size)
+
+    snapshot("init")
+    for i, act in enumerate(steps):
+        for obj in (c, sb, dk, bs):
+            obj.compact_batch(act)
+        snapshot(f"step{i}")
+    c.restore_full_batch()
+    out["restored_batch"] = np.int64(c.batch_size)
+    out["restored_shape"] = np.asarray(c.key_cache[0].shape, np.int64)
+    out["restored_all_zero"] = np.bool_(all(bool((t == 0).all()) for t in c.key_cache + c.value_cache) and
+                                        bool((c.cache_seqlens == 0).all()))
+    np.savez_compressed(HERE / "compaction.npz", **out)
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference()
@@ -221,6 +273,7 @@ def main():
     gen_rmsnorm(ref)
     gen_attention(ref)
     gen_index_ops(ref)
+    gen_compaction(ref)
     for p in sorted(HERE.glob("*.npz")):
         print(f"{p.name}: {p.stat().st_size / 1024:.1f} KiB")
 

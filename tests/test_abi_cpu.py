@@ -44,6 +44,6 @@ def test_torch_ops_meta_shapes():
     s = torch.empty(3, dtype=torch.int32, device=m)
     out = torch.ops.fdl.flash_kvcache(q, k, k, s, 0.088, False)
     assert out.shape == q.shape and out.dtype == q.dtype
-    for op in ("kv_append", "kv_scatter", "kv_gather_prefix", "kv_gather_rows", "kv_sparse_prefix",
+    for op in ("kv_append", "kv_scatter", "kv_gather_prefix", "kv_gather_rows", "kv_compact", "kv_sparse_prefix",
                "gather_rmsnorm", "block_attn"):
         assert hasattr(torch.ops.fdl, op)

@@ -60,3 +60,37 @@ def test_c_abi_argument_checks_return_before_device_work():
     strides = [0] * 12
     assert lib.fdl_block_attn(*args, 64, 0.125, *strides, 0, None, 0, None) == FDL_E_UNSUPPORTED  # head_dim 64
     assert lib.fdl_block_attn(*args[:12], 32, 27, 4, 128, 0.125, *strides, 0, None, 0, None) == FDL_E_SHAPE
+    lib.fdl_kv_compact.argtypes = [vp, i32, i64, i64, i32, vp, i32, vp]
+    lib.fdl_kv_compact.restype = i32
+    bufs = (ctypes.c_void_p * 2)(0x1000, 0x2000)
+    assert lib.fdl_kv_compact(None, 2, 64, 64, 4, None, 0, None) == FDL_OK  # nothing kept: nothing to move
+    assert lib.fdl_kv_compact(bufs, 2, 64, 64, 4, None, 3, None) == FDL_E_NULL
+    assert lib.fdl_kv_compact(bufs, 2, 64, 64, 4, fake, 5, None) == FDL_E_SHAPE  # more kept rows than slots
+    assert lib.fdl_kv_compact(bufs, 2, 64, 32, 4, fake, 3, None) == FDL_E_SHAPE  # rows would overlap
+    assert lib.fdl_kv_compact(bufs, 2, 64, 64, 5000, fake, 4097, None) == FDL_E_SHAPE  # list too long
+    assert lib.fdl_kv_compact(bufs, 2, 63, 63, 4, fake, 3, None) == 3  # FDL_E_ALIGN: odd row bytes
+
+
+def test_compaction_index_checks_run_on_the_host():
+    """compact_batch validates active_indices before any device work: the
+    in-place order needs i <= active_indices[i] < batch for every i."""
+    from fast_v2_b200.utils.compaction import active_rows, regrow
+
+    act = active_rows(torch.tensor([1, 2, 4], dtype=torch.int32), 5, "cpu")
+    assert act.dtype == torch.int64 and act.tolist() == [1, 2, 4]
+    assert active_rows([3, 1], 4, "cpu").tolist() == [3, 1]  # out of order but still in place-safe
+    assert active_rows(torch.empty(0, dtype=torch.long), 4, "cpu").numel() == 0
+    for bad, batch in (([1, 0], 4), ([0, 4], 4), ([0, 1, 2], 2)):
+        with pytest.raises(ValueError):
+            active_rows(torch.tensor(bad), batch, "cpu")
+    with pytest.raises(ValueError):
+        active_rows(torch.tensor([True, False, True]), 3, "cpu")
+    # regrow: a prefix view grows back over its own storage, zeroed
+    full = torch.arange(24, dtype=torch.float32).reshape(6, 4)
+    grown = regrow(full[:2], 6)
+    assert grown.data_ptr() == full.data_ptr() and grown.shape == (6, 4) and int(full.abs().sum()) == 0
+    lone = torch.ones(2, 4)
+    assert regrow(lone, 6).shape == (6, 4) and int(regrow(lone, 6).sum()) == 0
+    bsc = torch.ones(3, 5, 2)
+    g2 = regrow(bsc[:, :2], 5, dim=1)
+    assert g2.shape == (3, 5, 2) and g2.data_ptr() == bsc.data_ptr() and int(bsc.sum()) == 0

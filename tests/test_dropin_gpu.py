@@ -237,3 +237,85 @@ def test_patched_attention_forward_commit_and_scratch():
         assert_close(f"layer{l}", outs[l].float().cpu().numpy(), a.o_proj(ctx).float().cpu().numpy(), 5e-2, 5e-2)
     unpatch_attention_layers(m, orig)
     assert m.model.layers[0].self_attn.forward == orig[0]
+
+
+def test_compaction_of_every_cache_matches_reference_in_place():
+    """compact_batch twice (5 -> 3 -> 2 slots) on StaticKVCache,
+    StaticBlockCache, DynamicBlockKV and BlockSparseCache: the same bytes as
+    the reference's index_select compaction, with every buffer still at its
+    original address; restore_full_batch grows the views back, zeroed."""
+    g = golden("compaction")
+    L, (B, S, H, D) = 2, g["init_skv_k0"].shape
+    blk, hid = g["init_sbc_k0"].shape[1], g["init_bsc_layer_input"].shape[-1]
+    c = StaticKVCache(B, S, L, H, D, torch.bfloat16, DEV)
+    sb = StaticBlockCache(B, blk, L, H, D, torch.bfloat16, DEV)
+    dk = DynamicBlockKV(1, L + 1, B, H, blk, D, torch.bfloat16, DEV)
+    bs = BlockSparseCache(L, B, blk, hid, torch.bfloat16, DEV)
+    for l in range(L):
+        c.key_cache[l].copy_(t_from_bits(g[f"init_skv_k{l}"], DEV))
+        c.value_cache[l].copy_(t_from_bits(g[f"init_skv_v{l}"], DEV))
+        sb.key_cache[l].copy_(t_from_bits(g[f"init_sbc_k{l}"], DEV))
+        sb.value_cache[l].copy_(t_from_bits(g[f"init_sbc_v{l}"], DEV))
+    for l in dk.k:
+        dk.k[l].copy_(t_from_bits(g[f"init_dbk_k{l}"], DEV))
+        dk.v[l].copy_(t_from_bits(g[f"init_dbk_v{l}"], DEV))
+    names = ("layer_input", "attn_output", "mlp_input", "mlp_output")
+    for name in names:
+        getattr(bs, name).copy_(t_from_bits(g[f"init_bsc_{name}"], DEV))
+    c.cache_seqlens.copy_(torch.from_numpy(g["init_cache_seqlens"]))
+    c.scratch_seqlens.copy_(torch.from_numpy(g["init_scratch_seqlens"]))
+
+    def tensors():
+        return (c.key_cache + c.value_cache + sb.key_cache + sb.value_cache + list(dk.k.values()) +
+                list(dk.v.values()) + [getattr(bs, n) for n in names] + [c.cache_seqlens, c.scratch_seqlens])
+
+    ptrs = [t.data_ptr() for t in tensors()]
+    for i in range(2):
+        act = torch.from_numpy(g[f"active_{i}"]).to(DEV)
+        for obj in (c, sb, dk, bs):
+            obj.compact_batch(act)
+        tag = f"step{i}"
+        for l in range(L):
+            assert np.array_equal(bits_of(c.key_cache[l]), g[f"{tag}_skv_k{l}"])
+            assert np.array_equal(bits_of(c.value_cache[l]), g[f"{tag}_skv_v{l}"])
+            assert np.array_equal(bits_of(sb.key_cache[l]), g[f"{tag}_sbc_k{l}"])
+            assert np.array_equal(bits_of(sb.value_cache[l]), g[f"{tag}_sbc_v{l}"])
+        for l in dk.k:
+            assert np.array_equal(bits_of(dk.k[l]), g[f"{tag}_dbk_k{l}"])
+            assert np.array_equal(bits_of(dk.v[l]), g[f"{tag}_dbk_v{l}"])
+        for name in names:
+            assert np.array_equal(bits_of(getattr(bs, name)), g[f"{tag}_bsc_{name}"]), name
+        assert np.array_equal(c.cache_seqlens.cpu().numpy(), g[f"{tag}_cache_seqlens"])
+        assert np.array_equal(c.scratch_seqlens.cpu().numpy(), g[f"{tag}_scratch_seqlens"])
+        assert c.batch_size == sb.batch_size == dk.batch_size == bs.batch_size == int(g[f"{tag}_batch"])
+        assert [t.data_ptr() for t in tensors()] == ptrs
+    c.restore_full_batch()
+    assert c.batch_size == int(g["restored_batch"]) and list(c.key_cache[0].shape) == list(g["restored_shape"])
+    assert all(int(t.abs().max()) == 0 for t in c.key_cache + c.value_cache + [c.cache_seqlens])
+    assert [t.data_ptr() for t in c.key_cache + c.value_cache] == ptrs[:2 * L]
+
+
+def test_compaction_at_decode_size_and_refused_orders():
+    """A 16-slot cache of 2304 positions (the 7B geometry's KV heads) drops
+    5 finished slots: equal to index_select.  A list outside i <= a[i] is
+    refused: ValueError from the cache, and from the raw op nothing moves and
+    the device status names the offending entry."""
+    B, S, H, D, L = 16, 2304, 4, 128, 4
+    c = StaticKVCache(B, S, L, H, D, torch.bfloat16, DEV)
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    for t in c.key_cache + c.value_cache:
+        t.copy_(torch.randn(t.shape, generator=gen, device=DEV).to(torch.bfloat16))
+    c.cache_seqlens.copy_(torch.arange(B, dtype=torch.int32, device=DEV) * 100)
+    act = torch.tensor([0, 2, 3, 6, 7, 8, 10, 11, 13, 14, 15], device=DEV)
+    want = [t[act].clone() for t in c.key_cache + c.value_cache]
+    c.compact_batch(act)
+    for got, exp in zip(c.key_cache + c.value_cache, want):
+        assert torch.equal(got, exp)
+    assert torch.equal(c.cache_seqlens, act.to(torch.int32) * 100)
+    with pytest.raises(ValueError):
+        c.compact_batch(torch.tensor([1, 0], device=DEV))
+    buf = torch.arange(4 * 8, dtype=torch.float32, device=DEV).reshape(4, 8)
+    keep = buf.clone()
+    torch.ops.fdl.kv_compact([buf], torch.tensor([1, 0], device=DEV))
+    assert torch.equal(buf, keep)
+    assert _lib.last_device_error() == (1, 0)  # FDL_DEV_INDEX, active[1] = 0 < 1

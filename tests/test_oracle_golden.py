@@ -128,3 +128,53 @@ def test_sparse_prefix_spec_properties():
     # fp32 score close to a float64 norm
     ref = np.sqrt((O.bf16_to_f32(k).astype(np.float64) ** 2).sum(axis=(2, 3)))
     assert_close("score", score[0], ref[0], atol=1e-4, rtol=1e-5)
+
+
+_COMPACT_KEYS = ["skv_k0", "skv_v0", "skv_k1", "skv_v1", "sbc_k0", "sbc_v1", "dbk_k1", "dbk_v2"]
+
+
+def test_batch_compaction_matches_reference():
+    """Two compactions (5 -> 3 -> 2 slots) of every cache class: the
+    out-of-place restatement and the in-place order of the CUDA kernel both
+    give the reference's buffers."""
+    g = golden("compaction")
+    for key in _COMPACT_KEYS + ["cache_seqlens", "scratch_seqlens"]:
+        cur = g[f"init_{key}"]
+        inplace = cur.copy()
+        n = cur.shape[0]
+        for i in range(2):
+            act = g[f"active_{i}"]
+            cur = O.batch_compact(cur, act)
+            assert O.batch_compact_in_place(inplace[:n], act)
+            n = act.shape[0]
+            assert np.array_equal(cur, g[f"step{i}_{key}"]), (key, i)
+            assert np.array_equal(inplace[:n], g[f"step{i}_{key}"]), (key, i)
+    for name in ("layer_input", "attn_output", "mlp_input", "mlp_output"):
+        cur = g[f"init_bsc_{name}"]
+        for i in range(2):
+            cur = O.batch_compact(cur, g[f"active_{i}"], batch_axis=1)
+            assert np.array_equal(cur, g[f"step{i}_bsc_{name}"]), (name, i)
+    assert int(g["step1_batch"]) == 2 and int(g["restored_batch"]) == 5 and bool(g["restored_all_zero"])
+
+
+def test_in_place_compaction_order_property():
+    """For every list with i <= active[i] < batch (ascending distinct slots,
+    repeats, out-of-order lists such as [3, 1]) the sequential in-place order
+    equals the gather; every other list is refused with the buffer intact."""
+    rng = np.random.default_rng(5)
+    for trial in range(400):
+        B = int(rng.integers(1, 12))
+        buf = rng.integers(0, 1 << 16, size=(B, 6), dtype=np.uint16)
+        n = int(rng.integers(0, B + 1))
+        act = np.array([rng.integers(i, B) for i in range(n)], np.int64)
+        if trial % 4 == 0:
+            act = np.sort(rng.choice(B, size=n, replace=False)).astype(np.int64)
+        want = O.batch_compact(buf, act)
+        got = buf.copy()
+        assert O.batch_compact_in_place(got, act)
+        assert np.array_equal(got[:n], want)
+        assert np.array_equal(got[n:], buf[n:])  # rows past the kept ones are never written
+    for bad in ([1, 0], [0, 0], [2, 5]):
+        buf = np.arange(12, dtype=np.uint16).reshape(4, 3)
+        keep = buf.copy()
+        assert not O.batch_compact_in_place(buf, np.array(bad)) and np.array_equal(buf, keep)
