@@ -33,6 +33,9 @@ EXPORTS = (
     "fdl_rope_qkv",
     "fdl_swiglu",
     "fdl_add_rmsnorm",
+    "fdl_cosine_select",
+    "fdl_focus_select",
+    "fdl_focus_importance",
     "fdl_last_device_error",
     "fdl_version",
 )

@@ -12,6 +12,7 @@
 #include "sparse_prefix.cuh"
 #include "block_attn.cuh"
 #include "rope_swiglu.cuh"
+#include "token_select.cuh"
 
 using namespace fdl;
 
@@ -529,6 +530,70 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
   if (rc != FDL_OK || splits == 1) return rc;
   attn_combine_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(p.ws_o, p.ws_lse, p.out, splits, batch,
                                                                             sq, hq, o_sb, o_ss, o_sh);
+  return launch_status();
+}
+
+int fdl_cosine_select(const void* hidden, const void* cached, void* cache_out, int batch, int seq, int hidden_size,
+                      int dtype, int64_t h_sb, int64_t h_ss, int64_t c_sb, int64_t c_ss, int64_t o_sb, int64_t o_ss,
+                      int n_select, int64_t* idx, int64_t idx_sb, float* cos_out, fdl_stream_t stream) {
+  if (dtype != FDL_BF16 && dtype != FDL_F32) return FDL_E_DTYPE;
+  const int esz = dtype == FDL_BF16 ? 2 : 4;
+  if (batch < 0 || batch > 65535 || seq < 1 || seq > kSelMaxSeq || hidden_size < 1 ||
+      (hidden_size * esz) % 16 || n_select < 0 || n_select > seq || idx_sb < n_select)
+    return FDL_E_SHAPE;
+  if (batch == 0) return FDL_OK;
+  if (!hidden || !cached || (n_select > 0 && !idx)) return FDL_E_NULL;
+  for (int64_t st : {h_sb, h_ss, c_sb, c_ss, o_sb, o_ss})
+    if ((st * esz) % 16) return FDL_E_ALIGN;
+  if (!aligned16(hidden) || !aligned16(cached) || (cache_out && !aligned16(cache_out))) return FDL_E_ALIGN;
+  CosSelectArgs a{static_cast<const char*>(hidden), static_cast<const char*>(cached), static_cast<char*>(cache_out),
+                  h_sb * esz, h_ss * esz, c_sb * esz, c_ss * esz, o_sb * esz, o_ss * esz,
+                  seq, hidden_size, n_select, dtype == FDL_BF16, idx, idx_sb, cos_out};
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == FDL_BF16)
+    cosine_select_kernel<true><<<batch, kCosThreads, 0, s>>>(a);
+  else
+    cosine_select_kernel<false><<<batch, kCosThreads, 0, s>>>(a);
+  return launch_status();
+}
+
+int fdl_focus_select(const void* delta, int64_t delta_sb, const uint8_t* mask, int64_t mask_sb, const uint8_t* frozen,
+                     int64_t frozen_sb, int batch, int seq, int k_floor, int dtype, int64_t* sel, int64_t sel_sb,
+                     int32_t* ksel, fdl_stream_t stream) {
+  if (dtype != FDL_BF16 && dtype != FDL_F32) return FDL_E_DTYPE;
+  if (batch < 0 || batch > kFocusSelMaxRows || seq < 1 || seq > kSelMaxSeq || k_floor < 1 || k_floor > seq ||
+      sel_sb < seq)
+    return FDL_E_SHAPE;
+  if (batch == 0) return FDL_OK;
+  if (!delta || !mask || !sel || !ksel) return FDL_E_NULL;
+  const int esz = dtype == FDL_BF16 ? 2 : 4;
+  FocusSelectArgs a{static_cast<const char*>(delta), delta_sb * esz, mask, mask_sb, frozen, frozen_sb,
+                    batch, seq, k_floor, dtype == FDL_BF16, sel, sel_sb, ksel};
+  focus_select_kernel<<<1, kFocusSelThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+int fdl_focus_importance(const void* q, const void* k, const uint8_t* mask, int batch, int seq, int hq, int hkv,
+                         int head_dim, int dtype, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t k_sb, int64_t k_sh,
+                         int64_t k_ss, int64_t mask_sb, float scaling, void* imp, int64_t imp_sb,
+                         fdl_stream_t stream) {
+  if (dtype != FDL_BF16 && dtype != FDL_F32) return FDL_E_DTYPE;
+  const int esz = dtype == FDL_BF16 ? 2 : 4;
+  if (batch < 0 || batch > 65535 || seq < 1 || seq > kSelMaxSeq || hq < 1 || hq > kImpMaxHeads || hkv < 1 ||
+      hq % hkv || head_dim < 1 || head_dim > kImpMaxDim || (head_dim * esz) % 16)
+    return FDL_E_SHAPE;
+  if (batch == 0) return FDL_OK;
+  if (!q || !k || !mask || !imp) return FDL_E_NULL;
+  if (!aligned16(q) || (q_sb * esz) % 16 || (q_sh * esz) % 16 || (q_ss * esz) % 16) return FDL_E_ALIGN;
+  FocusImportanceArgs a{static_cast<const char*>(q), q_sb * esz, q_sh * esz, q_ss * esz,
+                        static_cast<const char*>(k), k_sb * esz, k_sh * esz, k_ss * esz,
+                        mask, mask_sb, seq, hq, hkv, head_dim, dtype == FDL_BF16, scaling,
+                        static_cast<char*>(imp), imp_sb * esz};
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == FDL_BF16)
+    focus_importance_kernel<true><<<batch, kImpThreads, 0, s>>>(a);
+  else
+    focus_importance_kernel<false><<<batch, kImpThreads, 0, s>>>(a);
   return launch_status();
 }
 

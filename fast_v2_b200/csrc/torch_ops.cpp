@@ -272,6 +272,84 @@ void kv_compact(at::TensorList bufs, const Tensor& active) {
            "kv_compact");
 }
 
+// ---------------------------------------------------------------- (a18)
+int select_dtype(const Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kFloat,
+              "fdl: token selection takes bf16 or fp32 inputs, got ", t.scalar_type());
+  return t.scalar_type() == at::kBFloat16 ? FDL_BF16 : FDL_F32;
+}
+
+void check_flags(const Tensor& t, int64_t B, int64_t S, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBool && t.dim() == 2 && t.size(0) == B && t.size(1) == S &&
+                  t.stride(1) == 1,
+              "fdl: ", name, " must be a CUDA bool [", B, ", ", S, "] tensor with unit inner stride");
+}
+
+void cosine_select(const Tensor& hidden, const Tensor& cached, int64_t n_select, bool refresh, const Tensor& idx,
+                   const std::optional<Tensor>& cos_out) {
+  check_cuda(hidden, "hidden");
+  check_cuda(cached, "cached");
+  TORCH_CHECK(hidden.dim() == 3 && cached.sizes() == hidden.sizes() && cached.dtype() == hidden.dtype(),
+              "fdl.cosine_select: hidden and cached are [B, S, H] of one dtype");
+  const int64_t B = hidden.size(0), S = hidden.size(1);
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kLong && idx.dim() == 2 && idx.size(0) == B &&
+                  idx.size(1) == n_select && idx.stride(1) == 1,
+              "fdl.cosine_select: idx must be a CUDA int64 [B, n_select] tensor with unit inner stride");
+  if (cos_out)
+    TORCH_CHECK(cos_out->is_cuda() && cos_out->scalar_type() == at::kFloat && cos_out->is_contiguous() &&
+                    cos_out->numel() == B * S,
+                "fdl.cosine_select: cos_out must be a contiguous CUDA fp32 [B, S] tensor");
+  c10::cuda::CUDAGuard guard(hidden.device());
+  check_rc(fdl_cosine_select(hidden.data_ptr(), cached.data_ptr(), refresh ? cached.data_ptr() : nullptr,
+                             static_cast<int>(B), static_cast<int>(S), static_cast<int>(hidden.size(2)),
+                             select_dtype(hidden), hidden.stride(0), hidden.stride(1), cached.stride(0),
+                             cached.stride(1), cached.stride(0), cached.stride(1), static_cast<int>(n_select),
+                             idx.data_ptr<int64_t>(), idx.stride(0), cos_out ? cos_out->data_ptr<float>() : nullptr,
+                             cur_stream()),
+           "cosine_select");
+}
+
+void focus_select(const Tensor& delta, const Tensor& mask, const std::optional<Tensor>& frozen, int64_t k_floor,
+                  const Tensor& sel, const Tensor& ksel) {
+  TORCH_CHECK(delta.is_cuda() && delta.dim() == 2 && delta.stride(1) == 1,
+              "fdl.focus_select: delta must be a CUDA [B, S] tensor with unit inner stride");
+  const int64_t B = delta.size(0), S = delta.size(1);
+  check_flags(mask, B, S, "mask");
+  if (frozen) check_flags(*frozen, B, S, "frozen");
+  TORCH_CHECK(sel.is_cuda() && sel.scalar_type() == at::kLong && sel.dim() == 2 && sel.size(0) == B &&
+                  sel.size(1) == S && sel.stride(1) == 1,
+              "fdl.focus_select: sel must be a CUDA int64 [B, S] tensor with unit inner stride");
+  TORCH_CHECK(ksel.is_cuda() && ksel.scalar_type() == at::kInt && ksel.numel() >= 1,
+              "fdl.focus_select: ksel must be a CUDA int32 tensor");
+  c10::cuda::CUDAGuard guard(delta.device());
+  check_rc(fdl_focus_select(delta.data_ptr(), delta.stride(0), reinterpret_cast<const uint8_t*>(mask.data_ptr()),
+                            mask.stride(0), frozen ? reinterpret_cast<const uint8_t*>(frozen->data_ptr()) : nullptr,
+                            frozen ? frozen->stride(0) : 0, static_cast<int>(B), static_cast<int>(S),
+                            static_cast<int>(k_floor), select_dtype(delta), sel.data_ptr<int64_t>(), sel.stride(0),
+                            ksel.data_ptr<int32_t>(), cur_stream()),
+           "focus_select");
+}
+
+void focus_importance(const Tensor& q, const Tensor& k, const Tensor& mask, double scaling, const Tensor& imp) {
+  check_cuda(q, "q");
+  check_cuda(k, "k");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && k.size(0) == q.size(0) && k.size(2) == q.size(2) &&
+                  k.size(3) == q.size(3) && k.dtype() == q.dtype(),
+              "fdl.focus_importance: q [B, Hq, S, D] and k [B, Hkv, S, D] of one dtype");
+  const int64_t B = q.size(0), S = q.size(2);
+  check_flags(mask, B, S, "mask");
+  TORCH_CHECK(imp.is_cuda() && imp.dim() == 2 && imp.size(0) == B && imp.size(1) == S && imp.stride(1) == 1 &&
+                  imp.dtype() == q.dtype(),
+              "fdl.focus_importance: imp must be a CUDA [B, S] tensor of q's dtype with unit inner stride");
+  c10::cuda::CUDAGuard guard(q.device());
+  check_rc(fdl_focus_importance(q.data_ptr(), k.data_ptr(), reinterpret_cast<const uint8_t*>(mask.data_ptr()),
+                                static_cast<int>(B), static_cast<int>(S), static_cast<int>(q.size(1)),
+                                static_cast<int>(k.size(1)), static_cast<int>(q.size(3)), select_dtype(q), q.stride(0),
+                                q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), mask.stride(0),
+                                static_cast<float>(scaling), imp.data_ptr(), imp.stride(0), cur_stream()),
+           "focus_importance");
+}
+
 void kv_sparse_prefix(const Tensor& k, const Tensor& v, const Tensor& lens, int64_t keep_num, int64_t keep_den,
                       const Tensor& sel, const Tensor& out_len, const std::optional<Tensor>& k_out,
                       const std::optional<Tensor>& v_out, const Tensor& workspace) {
@@ -508,6 +586,10 @@ TORCH_LIBRARY(fdl, m) {
   m.def("kv_gather_rows(Tensor k_src, Tensor? v_src, Tensor idx, Tensor? count, Tensor(a!) k_out, "
         "Tensor(b!)? v_out, int seq_dim) -> ()");
   m.def("kv_compact(Tensor(a!)[] bufs, Tensor active) -> ()");
+  m.def("cosine_select(Tensor hidden, Tensor(a!) cached, int n_select, bool refresh, Tensor(b!) idx, "
+        "Tensor(c!)? cos_out) -> ()");
+  m.def("focus_select(Tensor delta, Tensor mask, Tensor? frozen, int k_floor, Tensor(a!) sel, Tensor(b!) ksel) -> ()");
+  m.def("focus_importance(Tensor q, Tensor k, Tensor mask, float scaling, Tensor(a!) imp) -> ()");
   m.def("kv_sparse_prefix(Tensor k, Tensor v, Tensor lens, int keep_num, int keep_den, Tensor(a!) sel, "
         "Tensor(b!) out_len, Tensor(c!)? k_out, Tensor(d!)? v_out, Tensor(e!) workspace) -> ()");
   m.def("gather_rmsnorm(Tensor x, Tensor? idx, Tensor? weight, float eps, Tensor(a!)? gathered, "
@@ -528,6 +610,9 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("kv_gather_prefix", &kv_gather_prefix);
   m.impl("kv_gather_rows", &kv_gather_rows);
   m.impl("kv_compact", &kv_compact);
+  m.impl("cosine_select", &cosine_select);
+  m.impl("focus_select", &focus_select);
+  m.impl("focus_importance", &focus_importance);
   m.impl("kv_sparse_prefix", &kv_sparse_prefix);
   m.impl("gather_rmsnorm", &gather_rmsnorm);
   m.impl("block_attn", &block_attn);
@@ -547,6 +632,10 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
   m.impl("kv_gather_rows", [](const Tensor&, const std::optional<Tensor>&, const Tensor&,
                               const std::optional<Tensor>&, const Tensor&, const std::optional<Tensor>&, int64_t) {});
   m.impl("kv_compact", [](at::TensorList, const Tensor&) {});
+  m.impl("cosine_select", [](const Tensor&, const Tensor&, int64_t, bool, const Tensor&, const std::optional<Tensor>&) {});
+  m.impl("focus_select", [](const Tensor&, const Tensor&, const std::optional<Tensor>&, int64_t, const Tensor&,
+                            const Tensor&) {});
+  m.impl("focus_importance", [](const Tensor&, const Tensor&, const Tensor&, double, const Tensor&) {});
   m.impl("kv_sparse_prefix",
          [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
             const std::optional<Tensor>&, const std::optional<Tensor>&, const Tensor&) {});

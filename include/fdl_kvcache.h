@@ -318,6 +318,61 @@ int fdl_block_attn(const void* q, const void* k, const void* v,
                    fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Token selection feeding the sparse gathers (one block of seq <= 32 tokens
+ * per sequence).  Index outputs are exact: float reductions run in a fixed
+ * order, bf16 inputs (dtype FDL_BF16) are rounded to bf16 after every step
+ * where the reference's bf16 torch op rounds, FDL_F32 inputs are not; equal
+ * values rank by position, lower index first (torch.topk leaves that open).
+ * Strides are in elements; rows read as 16-byte vectors must be 16-byte
+ * aligned.
+ *
+ * fdl_cosine_select: for every sequence b and token s < seq,
+ *   cos[b, s] = sum_e (x_e / max(|x|, eps)) * (y_e / max(|y|, eps)),
+ *   x = hidden[b, s, :], y = cached[b, s, :], eps = 1e-8
+ * (F.cosine_similarity); idx[b, :n_select] = the n_select tokens of lowest
+ * cos, ascending.  With cache_out != NULL the hidden rows are then copied
+ * into cache_out (may be `cached` itself: each row is read before it is
+ * overwritten).  cos_out (fp32 [B, seq], optional) returns the similarities.
+ * hidden_size % (16 / element bytes) == 0.  Replaces the sparse forward's
+ * cosine top-k + sort and the layer-input cache refresh
+ * (modeling.py:868-877).
+ *
+ * fdl_focus_select: _focus_select (modeling.py:240-306) with the retain
+ * target k_floor = max(1, min(seq, ceil(...))) computed by the caller:
+ * mean + std threshold over the masked deltas, right-neighbour rule, top
+ * k_floor masked deltas, decoded tokens retained, frozen ones (optional)
+ * dropped; ksel[0] = the batch-uniform count; sel[b, :ksel] = the ksel
+ * highest-priority positions (retained first) ascending, sel[b, ksel:seq]
+ * = -1.  mask / frozen are bool (one byte) [B, seq].  batch <= 4096.
+ *
+ * fdl_focus_importance: _focus_importance (modeling.py:214-237): for every
+ * sequence the attention mass each masked key receives from masked queries
+ * (scores scaled, max-pooled over 3 keys, softmaxed over masked keys),
+ * summed over queries and heads.  q [B, hq, seq, D], k [B, hkv, seq, D]
+ * (query head h reads key head h / (hq / hkv): no repeat_kv copy); mask bool
+ * [B, seq]; imp [B, seq] in the input dtype.  hq <= 128, D <= 128.
+ * Floating point: within bf16 tolerance of the reference.
+ * ---------------------------------------------------------------------- */
+int fdl_cosine_select(const void* hidden, const void* cached, void* cache_out,
+                      int batch, int seq, int hidden_size, int dtype,
+                      int64_t h_sb, int64_t h_ss, int64_t c_sb, int64_t c_ss,
+                      int64_t o_sb, int64_t o_ss,
+                      int n_select, int64_t* idx, int64_t idx_sb, float* cos_out,
+                      fdl_stream_t stream);
+int fdl_focus_select(const void* delta, int64_t delta_sb,
+                     const uint8_t* mask, int64_t mask_sb,
+                     const uint8_t* frozen, int64_t frozen_sb,
+                     int batch, int seq, int k_floor, int dtype,
+                     int64_t* sel, int64_t sel_sb, int32_t* ksel,
+                     fdl_stream_t stream);
+int fdl_focus_importance(const void* q, const void* k, const uint8_t* mask,
+                         int batch, int seq, int hq, int hkv, int head_dim, int dtype,
+                         int64_t q_sb, int64_t q_sh, int64_t q_ss,
+                         int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                         int64_t mask_sb, float scaling,
+                         void* imp, int64_t imp_sb, fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Decode-forward elementwise stages next to the KV path (single HBM pass).
  *
  * fdl_rope_qkv: y is the fused q/k/v projection output, bf16

@@ -265,6 +265,75 @@ def gen_compaction(ref):
     np.savez_compressed(HERE / "compaction.npz", **out)
 
 
+def gen_select(ref):
+    """Token selection feeding the sparse gathers, run through the reference's
+    own code: _focus_importance (modeling.py:214-237), _focus_select
+    (modeling.py:240-306) and the cosine top-k of the sparse forward
+    (modeling.py:868-874), in bf16 and fp32.  torch.topk leaves the order of
+    equal values open, so the inputs are built without ties where the choice
+    matters: distinct deltas, frozen sets that never force frozen padding,
+    cosine targets spaced well apart."""
+    M = ref.modeling
+    g = torch.Generator().manual_seed(17)
+    out = {}
+    for tag, dt in (("bf16", torch.bfloat16), ("f32", torch.float32)):
+        # importance: the 7B head ratio (7 query heads per KV head), one row with nothing masked
+        B, Hkv, rep, S, D = 2, 2, 7, 32, 128
+        q = (torch.randn(B, Hkv * rep, S, D, generator=g) * 2.0).to(dt)
+        k = torch.randn(B, Hkv, S, D, generator=g).to(dt)
+        mask = torch.rand(B, S, generator=g) < 0.6
+        mask[1] = False
+        imp = M._focus_importance(q, M.repeat_kv(k, rep), mask, D ** -0.5)
+        conv = bits if dt == torch.bfloat16 else (lambda z: z.numpy())
+        out.update({f"imp_{tag}_q": conv(q), f"imp_{tag}_k": conv(k), f"imp_{tag}_mask": mask.numpy(),
+                    f"imp_{tag}_out": imp.float().numpy()})
+        # selection: distinct deltas (multiples of 2^-6), masks from sparse to full
+        n_sel = 0
+        for i in range(16):
+            Bs, S = 4, 32
+            vals = (torch.randperm(401, generator=g)[: Bs * S] - 200).float() / 64.0
+            delta = vals.reshape(Bs, S).to(dt)
+            mask = torch.rand(Bs, S, generator=g) < (0.15 + 0.05 * i)
+            frozen = None
+            if i % 3 == 1:
+                # the same number of frozen decoded slots in every row: no frozen padding
+                frozen = torch.zeros(Bs, S, dtype=torch.bool)
+                for b in range(Bs):
+                    dec = torch.nonzero(~mask[b]).flatten()
+                    frozen[b, dec[: min(2, dec.numel())]] = True
+                if len({int(f.sum()) for f in frozen}) != 1:
+                    frozen = None
+            avg, alpha = 1.0 + (i % 5), 1.0 + 0.5 * (i % 3)
+            ro = 0.75 if i % 7 == 6 else None
+            idx, ksel = M._focus_select(delta, mask, avg, alpha, ro, frozen=frozen)
+            pad = -np.ones((Bs, S), np.int64)
+            pad[:, :ksel] = idx.numpy()
+            key = f"sel_{tag}_{i}"
+            out.update({f"{key}_delta": conv(delta), f"{key}_mask": mask.numpy(),
+                        f"{key}_frozen": (frozen if frozen is not None else torch.zeros(Bs, S, dtype=torch.bool)).numpy(),
+                        f"{key}_has_frozen": np.bool_(frozen is not None),
+                        f"{key}_args": np.array([avg, alpha, np.nan if ro is None else ro]),
+                        f"{key}_idx": pad, f"{key}_ksel": np.int64(ksel)})
+            n_sel += 1
+        out[f"sel_{tag}_n"] = np.int64(n_sel)
+        # cosine top-k: per-token target similarities spaced 1/40 apart
+        B, S, H = 2, 32, 1024
+        x = torch.randn(B, S, H, generator=g)
+        z = torch.randn(B, S, H, generator=g)
+        xh = x / x.norm(dim=-1, keepdim=True)
+        z = z - (z * xh).sum(-1, keepdim=True) * xh
+        zh = z / z.norm(dim=-1, keepdim=True)
+        tgt = torch.stack([torch.randperm(S, generator=g) for _ in range(B)]).float() / 40.0 + 0.1
+        y = (tgt[..., None] * xh + (1 - tgt[..., None] ** 2).sqrt() * zh) * (1.0 + torch.rand(B, S, 1, generator=g))
+        hidden, cached = (x * 0.7).to(dt), y.to(dt)
+        cos = torch.nn.functional.cosine_similarity(hidden, cached, dim=-1)
+        n = int(0.25 * S)
+        sel = cos.topk(n, dim=-1, largest=False).indices.sort(dim=-1).values
+        out.update({f"cos_{tag}_hidden": conv(hidden), f"cos_{tag}_cached": conv(cached), f"cos_{tag}_n": np.int64(n),
+                    f"cos_{tag}_cos": cos.float().numpy(), f"cos_{tag}_idx": sel.numpy()})
+    np.savez_compressed(HERE / "select.npz", **out)
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference()
@@ -274,6 +343,7 @@ def main():
     gen_attention(ref)
     gen_index_ops(ref)
     gen_compaction(ref)
+    gen_select(ref)
     for p in sorted(HERE.glob("*.npz")):
         print(f"{p.name}: {p.stat().st_size / 1024:.1f} KiB")
 

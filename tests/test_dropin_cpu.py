@@ -69,6 +69,29 @@ def test_c_abi_argument_checks_return_before_device_work():
     assert lib.fdl_kv_compact(bufs, 2, 64, 32, 4, fake, 3, None) == FDL_E_SHAPE  # rows would overlap
     assert lib.fdl_kv_compact(bufs, 2, 64, 64, 5000, fake, 4097, None) == FDL_E_SHAPE  # list too long
     assert lib.fdl_kv_compact(bufs, 2, 63, 63, 4, fake, 3, None) == 3  # FDL_E_ALIGN: odd row bytes
+    # token selection: one block of <= 32 tokens, bf16 (0) or fp32 (2) only
+    lib.fdl_focus_select.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp]
+    lib.fdl_focus_select.restype = i32
+    assert lib.fdl_focus_select(None, 32, None, 32, None, 0, 0, 32, 4, 0, None, 32, None, None) == FDL_OK
+    assert lib.fdl_focus_select(None, 32, None, 32, None, 0, 2, 32, 4, 0, None, 32, None, None) == FDL_E_NULL
+    assert lib.fdl_focus_select(fake, 33, fake, 33, None, 0, 2, 33, 4, 0, fake, 33, fake, None) == FDL_E_SHAPE
+    assert lib.fdl_focus_select(fake, 32, fake, 32, None, 0, 2, 32, 0, 0, fake, 32, fake, None) == FDL_E_SHAPE
+    assert lib.fdl_focus_select(fake, 32, fake, 32, None, 0, 2, 32, 4, 1, fake, 32, fake, None) == 4  # FDL_E_DTYPE
+    lib.fdl_cosine_select.argtypes = [vp, vp, vp, i32, i32, i32, i32] + [i64] * 6 + [i32, vp, i64, vp, vp]
+    lib.fdl_cosine_select.restype = i32
+    st = [32 * 64, 64, 32 * 64, 64, 0, 0]
+    assert lib.fdl_cosine_select(fake, fake, None, 2, 32, 60, 0, *st, 8, fake, 8, None, None) == FDL_E_SHAPE
+    assert lib.fdl_cosine_select(fake, fake, None, 2, 32, 64, 0, *st, 33, fake, 33, None, None) == FDL_E_SHAPE
+    assert lib.fdl_cosine_select(None, fake, None, 2, 32, 64, 0, *st, 8, fake, 8, None, None) == FDL_E_NULL
+    assert lib.fdl_cosine_select(fake, fake, None, 2, 32, 64, 0, 32 * 64, 60, 32 * 64, 64, 0, 0, 8, fake, 8, None,
+                                 None) == 3  # FDL_E_ALIGN: token stride of 120 bytes
+    lib.fdl_focus_importance.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32] + [i64] * 7 + [ctypes.c_float, vp,
+                                                                                             i64, vp]
+    lib.fdl_focus_importance.restype = i32
+    ist = [0] * 7
+    assert lib.fdl_focus_importance(fake, fake, fake, 1, 32, 28, 3, 128, 0, *ist, 0.1, fake, 32, None) == FDL_E_SHAPE
+    assert lib.fdl_focus_importance(fake, fake, fake, 1, 32, 28, 4, 256, 0, *ist, 0.1, fake, 32, None) == FDL_E_SHAPE
+    assert lib.fdl_focus_importance(fake, fake, None, 1, 32, 28, 4, 128, 0, *ist, 0.1, fake, 32, None) == FDL_E_NULL
 
 
 def test_compaction_index_checks_run_on_the_host():
