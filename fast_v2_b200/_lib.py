@@ -31,6 +31,7 @@ EXPORTS = (
     "fdl_block_attn_auto_splits",
     "fdl_block_attn",
     "fdl_rope_qkv",
+    "fdl_rope_qkv_kv",
     "fdl_swiglu",
     "fdl_add_rmsnorm",
     "fdl_cosine_select",

@@ -604,9 +604,33 @@ int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* i
   if (rows == 0) return FDL_OK;
   if (!y || !pos || !inv_freq || !q || !k || !v) return FDL_E_NULL;
   if (!aligned16(y) || !aligned16(q) || !aligned16(k) || !aligned16(v) || (y_rs * 2) % 16) return FDL_E_ALIGN;
+  // Contiguous k / v [rows, hkv, D]: one "sequence" of `rows` tokens.
+  const int64_t rb = static_cast<int64_t>(head_dim) * 2;
   RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
-             static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), rows, hq, hkv, head_dim};
+             static_cast<char*>(k), static_cast<char*>(v), 0, hkv * rb, rb, nullptr, nullptr, 0,
+             rows, hq, hkv, head_dim, rows, rows};
   rope_qkv_kernel<<<rows, kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+int fdl_rope_qkv_kv(const void* y, int64_t y_rs, const int64_t* pos, const float* inv_freq, void* q, void* k_dst,
+                    void* v_dst, int64_t dst_sb, int64_t dst_ss, int64_t dst_sh, int dst_len, const int32_t* start,
+                    const int64_t* dst_pos, int64_t dst_pos_sb, int batch, int n, int hq, int hkv, int head_dim,
+                    fdl_stream_t stream) {
+  if (batch < 0 || batch > 65535 || n < 0 || hq < 1 || hkv < 1 || head_dim < 16 || head_dim % 16 ||
+      head_dim / 2 > kRopeMaxHalf || dst_len < 1 || (start && dst_pos))
+    return FDL_E_SHAPE;
+  const int64_t rows = static_cast<int64_t>(batch) * n;
+  if (rows == 0) return FDL_OK;
+  if (rows >= (1ll << 31)) return FDL_E_SHAPE;
+  if (!y || !pos || !inv_freq || !q || !k_dst || !v_dst) return FDL_E_NULL;
+  if (!aligned16(y) || !aligned16(q) || !aligned16(k_dst) || !aligned16(v_dst) || (y_rs * 2) % 16 ||
+      (dst_sb * 2) % 16 || (dst_ss * 2) % 16 || (dst_sh * 2) % 16)
+    return FDL_E_ALIGN;
+  RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
+             static_cast<char*>(k_dst), static_cast<char*>(v_dst), dst_sb * 2, dst_ss * 2, dst_sh * 2, start,
+             dst_pos, dst_pos_sb, static_cast<int>(rows), hq, hkv, head_dim, n, dst_len};
+  rope_qkv_kernel<<<static_cast<unsigned>(rows), kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 

@@ -6,7 +6,10 @@
 //                    after each multiply and after the add; cos/sin are
 //                    computed once per token (fp32 angle = pos * inv_freq,
 //                    rounded to bf16 like Fast_dLLM_QwenRotaryEmbedding,
-//                    modeling.py:545-560) and shared by every head.
+//                    modeling.py:545-560) and shared by every head.  K and V
+//                    are stored straight into their cache rows (append at a
+//                    per-sequence start, or scatter at given positions), so
+//                    no separate KV write follows the projection.
 //   swiglu_kernel    act = round(round(silu(gate)) * up) over the fused
 //                    gate/up projection output (Fast_dLLM_QwenMLP.forward,
 //                    modeling.py:163-165).
@@ -18,15 +21,23 @@ namespace fdl {
 constexpr int kRopeThreads = 256;
 constexpr int kRopeMaxHalf = 128;  // head_dim <= 256
 
+// Row r = b * T + t of y is token t of sequence b.  Its K and V rows go to
+// kd / vd + b * d_sb + p * d_ss + head * d_sh (bytes), at position
+// p = dpos[b, t] when dpos is set, else (start ? start[b] : 0) + t; a
+// position outside [0, d_len) skips that row's K/V and is reported.
 struct RopeArgs {
   const __nv_bfloat16* y;  // [rows, (hq + 2 hkv) * D]
   int64_t y_rs;            // row stride (elements)
-  const int64_t* pos;      // [rows]
+  const int64_t* pos;      // [rows] rotary positions
   const float* inv_freq;   // [D / 2]
   __nv_bfloat16* q;        // [rows, hq, D]
-  __nv_bfloat16* k;        // [rows, hkv, D]
-  __nv_bfloat16* v;        // [rows, hkv, D]
-  int rows, hq, hkv, D;
+  char* kd;                // K destination
+  char* vd;                // V destination
+  int64_t d_sb, d_ss, d_sh;  // bytes
+  const int32_t* start;    // [B] or null
+  const int64_t* dpos;     // [B, T] (row stride dpos_sb) or null
+  int64_t dpos_sb;
+  int rows, hq, hkv, D, T, d_len;
 };
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -42,6 +53,13 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qkv_kernel(const __grid_con
     s_cos[j] = bf16r(cs);
     s_sin[j] = bf16r(sn);
   }
+  const int b = row / a.T;
+  const int t = row - b * a.T;
+  const int64_t p_kv = a.dpos ? a.dpos[b * a.dpos_sb + t] : static_cast<int64_t>(a.start ? a.start[b] : 0) + t;
+  const bool store_kv = p_kv >= 0 && p_kv < a.d_len;
+  if (!store_kv && threadIdx.x == 0) report(FDL_DEV_INDEX, p_kv);
+  char* krow = a.kd + b * a.d_sb + (store_kv ? p_kv : 0) * a.d_ss;
+  char* vrow = a.vd + b * a.d_sb + (store_kv ? p_kv : 0) * a.d_ss;
   __syncthreads();
   const __nv_bfloat16* yr = a.y + static_cast<int64_t>(row) * a.y_rs;
   const int vpr = half / 8;                 // 8-element vectors per half row
@@ -67,16 +85,21 @@ __global__ void __launch_bounds__(kRopeThreads) rope_qkv_kernel(const __grid_con
         y1[e] = __float2bfloat16_rn(__fadd_rn(bf16r(__fmul_rn(a1, c)), bf16r(__fmul_rn(-a2, s))));
         y2[e] = __float2bfloat16_rn(__fadd_rn(bf16r(__fmul_rn(a2, c)), bf16r(__fmul_rn(a1, s))));
       }
-      __nv_bfloat16* dst = hh < a.hq ? a.q + (static_cast<int64_t>(row) * a.hq + hh) * a.D
-                                     : a.k + (static_cast<int64_t>(row) * a.hkv + (hh - a.hq)) * a.D;
-      *reinterpret_cast<uint4*>(dst + j0) = o1;
-      *reinterpret_cast<uint4*>(dst + half + j0) = o2;
-    } else {
+      if (hh < a.hq) {
+        __nv_bfloat16* dst = a.q + (static_cast<int64_t>(row) * a.hq + hh) * a.D;
+        *reinterpret_cast<uint4*>(dst + j0) = o1;
+        *reinterpret_cast<uint4*>(dst + half + j0) = o2;
+      } else if (store_kv) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(krow + (hh - a.hq) * a.d_sh);
+        *reinterpret_cast<uint4*>(dst + j0) = o1;
+        *reinterpret_cast<uint4*>(dst + half + j0) = o2;
+      }
+    } else if (store_kv) {
       const int vi = w - n_rope;
       const int hv = vi / (a.D / 8);
       const int d0 = (vi - hv * (a.D / 8)) * 8;
       const uint4 u = *reinterpret_cast<const uint4*>(yr + (a.hq + a.hkv + hv) * a.D + d0);
-      *reinterpret_cast<uint4*>(a.v + (static_cast<int64_t>(row) * a.hkv + hv) * a.D + d0) = u;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(vrow + hv * a.d_sh) + d0) = u;
     }
   }
 }

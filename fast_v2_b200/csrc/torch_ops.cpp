@@ -504,6 +504,52 @@ void rope_qkv(const Tensor& y, const Tensor& pos, const Tensor& inv_freq, int64_
            "rope_qkv");
 }
 
+// q/k/v split + RoPE with K and V stored straight into cache rows:
+// k_dst / v_dst are [B, S, H, D] (seq_dim 1) or [B, H, S, D] (seq_dim 2);
+// token t of sequence b goes to position dst_pos[b, t], or start[b] + t, or t.
+void rope_qkv_kv(const Tensor& y, const Tensor& pos, const Tensor& inv_freq, int64_t hq, int64_t hkv, const Tensor& q,
+                 const Tensor& k_dst, const Tensor& v_dst, const std::optional<Tensor>& start,
+                 const std::optional<Tensor>& dst_pos, int64_t seq_dim) {
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.stride(-1) == 1,
+              "fdl.rope_qkv_kv: y must be a bf16 CUDA tensor with unit inner stride");
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.scalar_type() == at::kBFloat16 && q.dim() == 4 &&
+                  q.size(2) == hq,
+              "fdl.rope_qkv_kv: q must be a contiguous bf16 CUDA [B, n, hq, D] tensor");
+  const int64_t B = q.size(0), n = q.size(1), D = q.size(3);
+  const int64_t rows = B * n;
+  TORCH_CHECK(y.numel() == rows * (hq + 2 * hkv) * D, "fdl.rope_qkv_kv: y must hold B*n rows of (hq+2hkv)*D");
+  TORCH_CHECK(y.dim() == 2 || (y.dim() == 3 && y.stride(0) == y.size(1) * y.stride(1)),
+              "fdl.rope_qkv_kv: y rows must be uniformly strided");
+  TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kLong && pos.is_contiguous() && pos.numel() == rows,
+              "fdl.rope_qkv_kv: pos must be a contiguous CUDA int64 tensor with one entry per row");
+  TORCH_CHECK(inv_freq.is_cuda() && inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == D / 2,
+              "fdl.rope_qkv_kv: inv_freq must be CUDA fp32 [D/2]");
+  check_cuda(k_dst, "k_dst");
+  check_cuda(v_dst, "v_dst");
+  const Rows d = rows_of(k_dst, seq_dim);
+  TORCH_CHECK(k_dst.scalar_type() == at::kBFloat16 && v_dst.sizes() == k_dst.sizes() &&
+                  v_dst.strides() == k_dst.strides() && v_dst.dtype() == k_dst.dtype(),
+              "fdl.rope_qkv_kv: k_dst and v_dst must be bf16 tensors of one shape and layout");
+  TORCH_CHECK(d.B == B && d.H == hkv && d.D == D, "fdl.rope_qkv_kv: destination ", k_dst.sizes(),
+              " does not hold [B, *, hkv, D] = [", B, ", *, ", hkv, ", ", D, "]");
+  TORCH_CHECK(!(start && dst_pos), "fdl.rope_qkv_kv: give start or dst_pos, not both");
+  if (start)
+    TORCH_CHECK(start->is_cuda() && start->scalar_type() == at::kInt && start->is_contiguous() && start->numel() == B,
+                "fdl.rope_qkv_kv: start must be a contiguous CUDA int32 [B] tensor");
+  if (dst_pos)
+    TORCH_CHECK(dst_pos->is_cuda() && dst_pos->scalar_type() == at::kLong && dst_pos->dim() == 2 &&
+                    dst_pos->size(0) == B && dst_pos->size(1) == n && dst_pos->stride(1) == 1,
+                "fdl.rope_qkv_kv: dst_pos must be a CUDA int64 [B, n] tensor with unit inner stride");
+  c10::cuda::CUDAGuard guard(y.device());
+  check_rc(fdl_rope_qkv_kv(y.data_ptr(), y.stride(-2), pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
+                           q.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), d.sb, d.ss, d.sh, static_cast<int>(d.S),
+                           start ? start->data_ptr<int32_t>() : nullptr,
+                           dst_pos ? dst_pos->data_ptr<int64_t>() : nullptr, dst_pos ? dst_pos->stride(0) : 0,
+                           static_cast<int>(B), static_cast<int>(n), static_cast<int>(hq), static_cast<int>(hkv),
+                           static_cast<int>(D), cur_stream()),
+           "rope_qkv_kv");
+}
+
 void swiglu(const Tensor& gu, const Tensor& out) {
   TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.stride(-1) == 1 && out.is_cuda() &&
                   out.scalar_type() == at::kBFloat16 && out.stride(-1) == 1,
@@ -600,6 +646,8 @@ TORCH_LIBRARY(fdl, m) {
         "bool causal) -> Tensor");
   m.def("rope_qkv(Tensor y, Tensor pos, Tensor inv_freq, int hq, int hkv, Tensor(a!) q, Tensor(b!) k, "
         "Tensor(c!) v) -> ()");
+  m.def("rope_qkv_kv(Tensor y, Tensor pos, Tensor inv_freq, int hq, int hkv, Tensor(a!) q, Tensor(b!) k_dst, "
+        "Tensor(c!) v_dst, Tensor? start, Tensor? dst_pos, int seq_dim) -> ()");
   m.def("swiglu(Tensor gu, Tensor(a!) out) -> ()");
   m.def("add_rmsnorm(Tensor x, Tensor res, Tensor? weight, float eps, Tensor(a!)? sum_out, Tensor(b!) normed) -> ()");
 }
@@ -618,6 +666,7 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("block_attn", &block_attn);
   m.impl("flash_kvcache", &flash_kvcache);
   m.impl("rope_qkv", &rope_qkv);
+  m.impl("rope_qkv_kv", &rope_qkv_kv);
   m.impl("swiglu", &swiglu);
   m.impl("add_rmsnorm", &add_rmsnorm);
 }
@@ -647,6 +696,8 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
   m.impl("flash_kvcache", &flash_kvcache_meta);
   m.impl("rope_qkv", [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
                         const Tensor&) {});
+  m.impl("rope_qkv_kv", [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
+                           const Tensor&, const std::optional<Tensor>&, const std::optional<Tensor>&, int64_t) {});
   m.impl("swiglu", [](const Tensor&, const Tensor&) {});
   m.impl("add_rmsnorm", [](const Tensor&, const Tensor&, const std::optional<Tensor>&, double,
                            const std::optional<Tensor>&, const Tensor&) {});

@@ -386,6 +386,19 @@ int fdl_focus_importance(const void* q, const void* k, const uint8_t* mask,
  * (utils/attention_backends.py:777-788, 829-836) / apply_rotary_pos_emb
  * (modeling.py:186-199) with the rotary table of modeling.py:545-560.
  *
+ * fdl_rope_qkv_kv: the same split + rotary embedding for `batch` sequences
+ * of n tokens (row b * n + t of y), with q written contiguously and K / V
+ * written straight into their cache rows instead of separate buffers:
+ *   k_dst[b, p, h, :] / v_dst[b, p, h, :]  (element strides dst_sb, dst_ss,
+ *   dst_sh, so BSHD caches and BHSD block buffers both fit)
+ *   p = dst_pos[b, t] (int64, row stride dst_pos_sb) when dst_pos != NULL,
+ *   else start[b] + t (int32) when start != NULL, else t.
+ * Rows whose p falls outside [0, dst_len) store no K/V and are reported as
+ * FDL_DEV_INDEX.  Fuses the commit append (StaticKVCache.update /
+ * write_sparse at cache_seqlens + arange, utils/static_kv_cache.py:132-160,
+ * 231-247) and the block-buffer writes (DynamicBlockKV.write_full / write,
+ * utils/dynamic_block_kv.py:34-43) into the RoPE pass after the q/k/v GEMM.
+ *
  * fdl_swiglu: gu bf16 [rows, 2F] (gate then up, row stride gu_rs) ->
  * out [rows, F] (row stride out_rs) = bf16(bf16(silu(gate)) * up)
  * (Fast_dLLM_QwenMLP.forward, modeling.py:163-165).  F % 8 == 0.
@@ -393,6 +406,12 @@ int fdl_focus_importance(const void* q, const void* k, const uint8_t* mask,
 int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos,
                  const float* inv_freq, void* q, void* k, void* v,
                  int rows, int hq, int hkv, int head_dim, fdl_stream_t stream);
+int fdl_rope_qkv_kv(const void* y, int64_t y_rs, const int64_t* pos,
+                    const float* inv_freq, void* q, void* k_dst, void* v_dst,
+                    int64_t dst_sb, int64_t dst_ss, int64_t dst_sh, int dst_len,
+                    const int32_t* start, const int64_t* dst_pos, int64_t dst_pos_sb,
+                    int batch, int n, int hq, int hkv, int head_dim,
+                    fdl_stream_t stream);
 int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs,
                int64_t rows, int ffn, fdl_stream_t stream);
 

@@ -45,6 +45,6 @@ def test_torch_ops_meta_shapes():
     out = torch.ops.fdl.flash_kvcache(q, k, k, s, 0.088, False)
     assert out.shape == q.shape and out.dtype == q.dtype
     for op in ("kv_append", "kv_scatter", "kv_gather_prefix", "kv_gather_rows", "kv_compact", "kv_sparse_prefix",
-               "cosine_select", "focus_select", "focus_importance",
+               "cosine_select", "focus_select", "focus_importance", "rope_qkv_kv",
                "gather_rmsnorm", "block_attn"):
         assert hasattr(torch.ops.fdl, op)

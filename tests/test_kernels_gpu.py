@@ -340,6 +340,62 @@ def test_rope_qkv_matches_reference_rounding():
         assert frac < 2e-3 and worst <= 2.0, (name, frac, worst)
 
 
+def test_rope_qkv_kv_stores_into_cache_rows_like_rope_then_append_or_scatter():
+    """The fused RoPE + K/V store equals rope_qkv followed by the separate
+    append (BSHD cache at per-sequence starts) or scatter (BHSD block buffer
+    at given positions), bit for bit; q is identical too."""
+    B, n, hq, hkv, D, S = 3, 32, 28, 4, 128, 160
+    rows = B * n
+    y = rbf16((rows, (hq + 2 * hkv) * D), 81).to(DEV)
+    pos = torch.randint(0, 4096, (rows,), generator=torch.Generator().manual_seed(5)).to(DEV)
+    inv = (1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))).to(DEV)
+    q0 = torch.empty(rows, hq, D, dtype=torch.bfloat16, device=DEV)
+    k0 = torch.empty(rows, hkv, D, dtype=torch.bfloat16, device=DEV)
+    v0 = torch.empty_like(k0)
+    torch.ops.fdl.rope_qkv(y, pos, inv, hq, hkv, q0, k0, v0)
+    k0, v0 = k0.view(B, n, hkv, D), v0.view(B, n, hkv, D)
+    # (1) BSHD cache, append at per-sequence starts
+    start = torch.tensor([0, 37, S - n], dtype=torch.int32, device=DEV)
+    kc, vc = rbf16((B, S, hkv, D), 82).to(DEV), rbf16((B, S, hkv, D), 83).to(DEV)
+    ke, ve = kc.clone(), vc.clone()
+    torch.ops.fdl.kv_append([ke], [ve], [k0], [v0], start)
+    q = torch.empty(B, n, hq, D, dtype=torch.bfloat16, device=DEV)
+    torch.ops.fdl.rope_qkv_kv(y, pos, inv, hq, hkv, q, kc, vc, start, None, 1)
+    assert torch.equal(q.view(rows, hq, D), q0) and torch.equal(kc, ke) and torch.equal(vc, ve)
+    # (2) BHSD block buffer, all positions 0..n-1
+    bk, bv = rbf16((B, hkv, n, D), 84).to(DEV), rbf16((B, hkv, n, D), 85).to(DEV)
+    torch.ops.fdl.rope_qkv_kv(y, pos, inv, hq, hkv, q, bk, bv, None, None, 2)
+    assert torch.equal(bk, k0.transpose(1, 2)) and torch.equal(bv, v0.transpose(1, 2))
+    # (3) BHSD block buffer, scatter of 8 tokens per sequence at given positions
+    m = 8
+    ym = y.view(B, n, -1)[:, :m].reshape(B * m, -1).contiguous()
+    pm = pos.view(B, n)[:, :m].reshape(-1).contiguous()
+    fed = torch.stack([torch.randperm(n, generator=torch.Generator().manual_seed(10 + b))[:m] for b in range(B)])
+    fed = fed.to(DEV)
+    bk2, bv2 = bk.clone(), bv.clone()
+    torch.ops.fdl.kv_scatter(bk2, bv2, k0[:, :m].transpose(1, 2), v0[:, :m].transpose(1, 2), fed, 2)
+    qm = torch.empty(B, m, hq, D, dtype=torch.bfloat16, device=DEV)
+    torch.ops.fdl.rope_qkv_kv(ym, pm, inv, hq, hkv, qm, bk, bv, None, fed, 2)
+    assert torch.equal(bk, bk2) and torch.equal(bv, bv2)
+    assert torch.equal(qm, q0.view(B, n, hq, D)[:, :m])
+
+
+def test_rope_qkv_kv_position_past_the_cache_is_skipped_and_reported():
+    B, n, hq, hkv, D, S = 2, 4, 28, 4, 128, 8
+    y = rbf16((B * n, (hq + 2 * hkv) * D), 86).to(DEV)
+    pos = torch.arange(B * n, device=DEV)
+    inv = torch.ones(D // 2, device=DEV)
+    kc = torch.zeros(B, S, hkv, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(B, n, hq, D, dtype=torch.bfloat16, device=DEV)
+    start = torch.tensor([0, S - 2], dtype=torch.int32, device=DEV)  # tokens 2, 3 of sequence 1 fall outside
+    torch.ops.fdl.rope_qkv_kv(y, pos, inv, hq, hkv, q, kc, vc, start, None, 1)
+    code, info = _lib.last_device_error()
+    assert code == 1 and info in (S, S + 1)
+    assert bool((kc[0, :n] != 0).any()) and bool((kc[1, S - 2:] != 0).any())
+    assert int((kc[1, : S - 2] != 0).sum()) == 0
+
+
 def test_swiglu_matches_reference_rounding():
     rows, F_ = 257, 18944
     gu = rbf16((rows, 2 * F_), 71, 3.0)
