@@ -134,20 +134,6 @@ class BlockDiffusionLM:
         _lib.count_launches(1)
         return q, k, v
 
-    def qkv_into(self, layer, x, pos, k_dst, v_dst, start=None, dst_pos=None, seq_dim: int = 1):
-        """As ``qkv``, but K and V go straight into their cache rows: k_dst /
-        v_dst [B, S, Hkv, D] (seq_dim 1) or [B, Hkv, S, D] (seq_dim 2), token
-        t of sequence b at dst_pos[b, t], else start[b] + t, else t.  One
-        kernel after the GEMM; returns q."""
-        g = self.geo
-        B, T, _ = x.shape
-        y = torch.addmm(layer["bqkv"], x.view(B * T, -1), layer["wqkv"].t())
-        q = torch.empty(B, T, g.heads, g.head_dim, dtype=self.dtype, device=self.device)
-        torch.ops.fdl.rope_qkv_kv(y, pos.reshape(-1), self.inv_freq, g.heads, g.kv_heads, q, k_dst, v_dst, start,
-                                  dst_pos, seq_dim)
-        _lib.count_launches(1)
-        return q
-
     def add_rmsnorm(self, y, h, w):
         """Residual connection and the following RMSNorm in one kernel:
         h += y in place (bf16 rounding, the layer's `residual + hidden_states`)
@@ -203,6 +189,7 @@ class DecodeState:
         self.blk_k = [torch.zeros(batch, g.kv_heads, block, g.head_dim, dtype=dt, device=dev) for _ in range(g.layers)]
         self.blk_v = [torch.zeros_like(t) for t in self.blk_k]
         self.lens = torch.zeros(batch, dtype=torch.int32, device=dev)  # committed length per sequence
+        self.zero = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.sparse_keep = sparse_keep
         if sparse_keep:
             self.keep_num, self.keep_den = float(sparse_keep).as_integer_ratio()
@@ -220,21 +207,19 @@ class DecodeState:
         self.attn_ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev) if wsb > 0 else None
 
     # -------------------------------------------------------------- pieces
-    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos, lens=None):
+    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos):
         """Block attention for layer l: queries q [B, T, Hq, D] over the
-        committed prefix ("full", the first `lens` rows of the cache, default
-        self.lens) or the sparse prefix ("sparse") followed by the given block
-        K/V (none when k_blk is None), under the block-causal mask."""
+        committed prefix ("full") or the sparse prefix ("sparse") followed by
+        the given block K/V, under the block-causal mask."""
         g = self.model.geo
         out = torch.empty_like(q)
         if prefix == "sparse":
             kp, vp, lens = self.sp_k[l], self.sp_v[l], self.sp_len[l]
         else:
-            kp, vp, lens = self.k[l], self.v[l], self.lens if lens is None else lens
+            kp, vp, lens = self.k[l], self.v[l], self.lens
         T = q.shape[1]
-        n_blk = 0 if k_blk is None else k_blk.shape[1]
         ns = self.attn_splits if T <= self.block else _lib.attn_auto_splits(self.B, T, g.heads, g.kv_heads,
-                                                                            kp.shape[1], n_blk)
+                                                                            kp.shape[1], k_blk.shape[1])
         ws = self.attn_ws
         if ns > 1 and (ws is None or ws.numel() < _lib.attn_workspace_bytes(self.B, T, g.heads, ns)):
             ws = torch.empty(_lib.attn_workspace_bytes(self.B, T, g.heads, ns), dtype=torch.uint8, device=q.device)
@@ -263,14 +248,13 @@ class DecodeState:
         h = F.embedding(ids, m.embed)
         pos = pos.contiguous()
         qpos = pos.to(torch.int32).contiguous()
-        # The span's K/V are stored into the cache at self.lens by the RoPE
-        # kernel itself; the attention then reads cache[:lens + T] under the
-        # block-causal mask (the same keys as prefix + span).
-        lens_after = self.lens + T
 
         def attend_layer(l, layer, x):
-            q = m.qkv_into(layer, x, pos, self.k[l], self.v[l], start=self.lens)
-            return self.attend(q, l, "full", None, None, qpos, lens=lens_after)
+            q, k, v = m.qkv(layer, x, pos)
+            a = self.attend(q, l, "full", k, v, qpos)
+            torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
+            _lib.count_launches(1)
+            return a
 
         h = m.layers_forward(h, attend_layer)
         self.lens += T
@@ -298,10 +282,13 @@ class DecodeState:
         qpos = p.to(torch.int32).contiguous()
 
         def attend_layer(l, layer, x):
-            # K/V of the computed positions go straight into the block buffer
-            # (BHSD): positions 0..blk-1 on a full step, fed[b, i] on a cached one.
+            q, k, v = m.qkv(layer, x, p)
             bk, bv = self.blk_k[l], self.blk_v[l]
-            q = m.qkv_into(layer, x, p, bk, bv, dst_pos=fed, seq_dim=2)
+            if fed is None:
+                torch.ops.fdl.kv_append([bk.transpose(1, 2)], [bv.transpose(1, 2)], [k], [v], self.zero)
+            else:
+                torch.ops.fdl.kv_scatter(bk, bv, k.transpose(1, 2), v.transpose(1, 2), fed, 2)
+            _lib.count_launches(1)
             return self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
 
         h = m.layers_forward(h, attend_layer)

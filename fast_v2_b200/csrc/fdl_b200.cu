@@ -604,11 +604,8 @@ int fdl_rope_qkv(const void* y, int64_t y_rs, const int64_t* pos, const float* i
   if (rows == 0) return FDL_OK;
   if (!y || !pos || !inv_freq || !q || !k || !v) return FDL_E_NULL;
   if (!aligned16(y) || !aligned16(q) || !aligned16(k) || !aligned16(v) || (y_rs * 2) % 16) return FDL_E_ALIGN;
-  // Contiguous k / v [rows, hkv, D]: one "sequence" of `rows` tokens.
-  const int64_t rb = static_cast<int64_t>(head_dim) * 2;
   RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
-             static_cast<char*>(k), static_cast<char*>(v), 0, hkv * rb, rb, nullptr, nullptr, 0,
-             rows, hq, hkv, head_dim, rows, rows};
+             static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), rows, hq, hkv, head_dim};
   rope_qkv_kernel<<<rows, kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
@@ -627,10 +624,10 @@ int fdl_rope_qkv_kv(const void* y, int64_t y_rs, const int64_t* pos, const float
   if (!aligned16(y) || !aligned16(q) || !aligned16(k_dst) || !aligned16(v_dst) || (y_rs * 2) % 16 ||
       (dst_sb * 2) % 16 || (dst_ss * 2) % 16 || (dst_sh * 2) % 16)
     return FDL_E_ALIGN;
-  RopeArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
-             static_cast<char*>(k_dst), static_cast<char*>(v_dst), dst_sb * 2, dst_ss * 2, dst_sh * 2, start,
-             dst_pos, dst_pos_sb, static_cast<int>(rows), hq, hkv, head_dim, n, dst_len};
-  rope_qkv_kernel<<<static_cast<unsigned>(rows), kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  RopeStoreArgs a{static_cast<const __nv_bfloat16*>(y), y_rs, pos, inv_freq, static_cast<__nv_bfloat16*>(q),
+                  static_cast<char*>(k_dst), static_cast<char*>(v_dst), dst_sb * 2, dst_ss * 2, dst_sh * 2, start,
+                  dst_pos, dst_pos_sb, static_cast<int>(rows), hq, hkv, head_dim, n, dst_len};
+  rope_qkv_store_kernel<<<static_cast<unsigned>(rows), kRopeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 

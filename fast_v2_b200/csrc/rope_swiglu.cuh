@@ -6,10 +6,11 @@
 //                    after each multiply and after the add; cos/sin are
 //                    computed once per token (fp32 angle = pos * inv_freq,
 //                    rounded to bf16 like Fast_dLLM_QwenRotaryEmbedding,
-//                    modeling.py:545-560) and shared by every head.  K and V
-//                    are stored straight into their cache rows (append at a
-//                    per-sequence start, or scatter at given positions), so
-//                    no separate KV write follows the projection.
+//                    modeling.py:545-560) and shared by every head.
+//   rope_qkv_store_kernel  the same split + rotary embedding with K and V
+//                    stored straight into their cache rows (append at a
+//                    per-sequence start, or scatter at given positions),
+//                    so no separate KV write follows the projection.
 //   swiglu_kernel    act = round(round(silu(gate)) * up) over the fused
 //                    gate/up projection output (Fast_dLLM_QwenMLP.forward,
 //                    modeling.py:163-165).
@@ -21,11 +22,74 @@ namespace fdl {
 constexpr int kRopeThreads = 256;
 constexpr int kRopeMaxHalf = 128;  // head_dim <= 256
 
+struct RopeArgs {
+  const __nv_bfloat16* y;  // [rows, (hq + 2 hkv) * D]
+  int64_t y_rs;            // row stride (elements)
+  const int64_t* pos;      // [rows]
+  const float* inv_freq;   // [D / 2]
+  __nv_bfloat16* q;        // [rows, hq, D]
+  __nv_bfloat16* k;        // [rows, hkv, D]
+  __nv_bfloat16* v;        // [rows, hkv, D]
+  int rows, hq, hkv, D;
+};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__global__ void __launch_bounds__(kRopeThreads) rope_qkv_kernel(const __grid_constant__ RopeArgs a) {
+  __shared__ float s_cos[kRopeMaxHalf], s_sin[kRopeMaxHalf];
+  const int row = blockIdx.x;
+  const int half = a.D / 2;
+  const float p = static_cast<float>(a.pos[row]);
+  for (int j = threadIdx.x; j < half; j += kRopeThreads) {
+    float sn, cs;
+    sincosf(__fmul_rn(p, a.inv_freq[j]), &sn, &cs);
+    s_cos[j] = bf16r(cs);
+    s_sin[j] = bf16r(sn);
+  }
+  __syncthreads();
+  const __nv_bfloat16* yr = a.y + static_cast<int64_t>(row) * a.y_rs;
+  const int vpr = half / 8;                 // 8-element vectors per half row
+  const int n_rope = (a.hq + a.hkv) * vpr;  // q and k heads
+  const int n_v = a.hkv * (a.D / 8);        // v copy vectors
+  for (int w = threadIdx.x; w < n_rope + n_v; w += kRopeThreads) {
+    if (w < n_rope) {
+      const int hh = w / vpr;
+      const int j0 = (w - hh * vpr) * 8;
+      const __nv_bfloat16* src = yr + hh * a.D;
+      const uint4 u1 = *reinterpret_cast<const uint4*>(src + j0);
+      const uint4 u2 = *reinterpret_cast<const uint4*>(src + half + j0);
+      const __nv_bfloat16* x1 = reinterpret_cast<const __nv_bfloat16*>(&u1);
+      const __nv_bfloat16* x2 = reinterpret_cast<const __nv_bfloat16*>(&u2);
+      uint4 o1, o2;
+      __nv_bfloat16* y1 = reinterpret_cast<__nv_bfloat16*>(&o1);
+      __nv_bfloat16* y2 = reinterpret_cast<__nv_bfloat16*>(&o2);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float c = s_cos[j0 + e], s = s_sin[j0 + e];
+        const float a1 = __bfloat162float(x1[e]), a2 = __bfloat162float(x2[e]);
+        // x * cos + rotate_half(x) * sin, rotate_half = cat(-x2, x1)
+        y1[e] = __float2bfloat16_rn(__fadd_rn(bf16r(__fmul_rn(a1, c)), bf16r(__fmul_rn(-a2, s))));
+        y2[e] = __float2bfloat16_rn(__fadd_rn(bf16r(__fmul_rn(a2, c)), bf16r(__fmul_rn(a1, s))));
+      }
+      __nv_bfloat16* dst = hh < a.hq ? a.q + (static_cast<int64_t>(row) * a.hq + hh) * a.D
+                                     : a.k + (static_cast<int64_t>(row) * a.hkv + (hh - a.hq)) * a.D;
+      *reinterpret_cast<uint4*>(dst + j0) = o1;
+      *reinterpret_cast<uint4*>(dst + half + j0) = o2;
+    } else {
+      const int vi = w - n_rope;
+      const int hv = vi / (a.D / 8);
+      const int d0 = (vi - hv * (a.D / 8)) * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(yr + (a.hq + a.hkv + hv) * a.D + d0);
+      *reinterpret_cast<uint4*>(a.v + (static_cast<int64_t>(row) * a.hkv + hv) * a.D + d0) = u;
+    }
+  }
+}
+
 // Row r = b * T + t of y is token t of sequence b.  Its K and V rows go to
 // kd / vd + b * d_sb + p * d_ss + head * d_sh (bytes), at position
 // p = dpos[b, t] when dpos is set, else (start ? start[b] : 0) + t; a
 // position outside [0, d_len) skips that row's K/V and is reported.
-struct RopeArgs {
+struct RopeStoreArgs {
   const __nv_bfloat16* y;  // [rows, (hq + 2 hkv) * D]
   int64_t y_rs;            // row stride (elements)
   const int64_t* pos;      // [rows] rotary positions
@@ -40,9 +104,8 @@ struct RopeArgs {
   int rows, hq, hkv, D, T, d_len;
 };
 
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__global__ void __launch_bounds__(kRopeThreads) rope_qkv_kernel(const __grid_constant__ RopeArgs a) {
+__global__ void __launch_bounds__(kRopeThreads) rope_qkv_store_kernel(const __grid_constant__ RopeStoreArgs a) {
   __shared__ float s_cos[kRopeMaxHalf], s_sin[kRopeMaxHalf];
   const int row = blockIdx.x;
   const int half = a.D / 2;
