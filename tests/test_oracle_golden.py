@@ -178,3 +178,21 @@ def test_in_place_compaction_order_property():
         buf = np.arange(12, dtype=np.uint16).reshape(4, 3)
         keep = buf.copy()
         assert not O.batch_compact_in_place(buf, np.array(bad)) and np.array_equal(buf, keep)
+
+
+def test_decoder_fed_indices_match_reference():
+    """The decoder's device-side _dkv_fed_indices (plain torch ops, run here on
+    CPU tensors) against the reference's outputs: same indices and width, and
+    with a fixed width the same rows padded further with the first index."""
+    import torch
+
+    from fast_v2_b200.block_decode import dkv_fed_indices
+
+    g = golden("index_ops")
+    for i in range(6):
+        prv = torch.from_numpy(g[f"fed_prv_{i}"])
+        fed, n = dkv_fed_indices(prv)
+        assert n == int(g[f"fed_n_{i}"]) and np.array_equal(fed.numpy(), g[f"fed_idx_{i}"]), i
+        wide, w = dkv_fed_indices(prv, 32)
+        assert w == 32 and np.array_equal(wide[:, :n].numpy(), g[f"fed_idx_{i}"]), i
+        assert np.all(wide[:, n:].numpy() == g[f"fed_idx_{i}"][:, :1]), i
