@@ -99,3 +99,51 @@ def test_equal_values_rank_by_position():
     assert SO.rank_select(v, 2, largest=True)[0].tolist() == [False, True, True, False, False]
     assert SO.rank_select(v, 3, largest=False)[0].tolist() == [True, True, False, True, False]
     assert SO.butterfly_sum(np.arange(32, dtype=np.float32)[None])[0] == 496.0
+
+
+def test_focus_select_invariants_on_random_blocks():
+    """Properties _focus_select guarantees (modeling.py:240-306): every
+    decoded, non-frozen token is kept; Ksel >= the retain target (unless
+    frozen tokens cap it); indices ascend without repeats; frozen tokens only
+    appear as padding once every non-frozen token is in."""
+    rng = np.random.default_rng(12)
+    for trial in range(300):
+        B, S = 3, 32
+        bf = trial % 2 == 0
+        d = SO.rnd(rng.standard_normal((B, S)).astype(np.float32) * 0.5, bf)
+        mask = rng.random((B, S)) < rng.random()
+        frozen = (rng.random((B, S)) < 0.3) & ~mask if trial % 3 == 0 else None
+        K = SO.focus_retain_k(S, 1.0 + trial % 6, 1.5)
+        idx, ksel = SO.focus_select(d, mask, K, bf, frozen)
+        assert idx.shape == (B, ksel) and 1 <= ksel <= S
+        if frozen is None:
+            assert ksel >= K
+        for b in range(B):
+            row = idx[b].tolist()
+            assert row == sorted(set(row))
+            fz = frozen[b] if frozen is not None else np.zeros(S, bool)
+            keep = set(np.nonzero(~mask[b] & ~fz)[0].tolist())
+            assert keep.issubset(row), (trial, b)
+            if any(fz[i] for i in row):
+                assert set(np.nonzero(~fz)[0].tolist()).issubset(row), (trial, b)
+
+
+def test_cosine_select_invariants():
+    """The selection holds the n lowest similarities (ties by position) and
+    a token identical to its cached input is never chosen before a changed one."""
+    rng = np.random.default_rng(13)
+    for trial in range(20):
+        B, S, H = 2, 32, 256
+        bf = trial % 2 == 0
+        h = SO.rnd(rng.standard_normal((B, S, H)).astype(np.float32), bf)
+        c = h.copy()
+        moved = rng.random((B, S)) < 0.3
+        c[moved] = SO.rnd(rng.standard_normal((int(moved.sum()), H)).astype(np.float32), bf)
+        n = int(rng.integers(1, S))
+        idx, cos = SO.cosine_select(h, c, n, bf)
+        for b in range(B):
+            sel = set(idx[b].tolist())
+            worst = max(cos[b, list(sel)])
+            assert all(cos[b, i] >= worst for i in range(S) if i not in sel)
+            if n <= int(moved[b].sum()):
+                assert sel.issubset(set(np.nonzero(moved[b])[0].tolist())), (trial, b)
