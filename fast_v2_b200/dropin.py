@@ -7,6 +7,10 @@ modules on the hot path) resolve to the B200 implementations, so the
 reference's generation_functions.py and eval.py drive them unchanged.  Modules
 of the reference that are not on the hot path (utils.batch_bucketing,
 utils.dynamo_utils, the model) keep resolving to the reference's own files.
+
+The FOCUS token selection lives in module-level helpers of the model file
+(modeling.py:214-306); ``patch_modeling(modeling)`` points those names at the
+GPU versions in ``fast_v2_b200.focus`` and returns the originals.
 """
 from __future__ import annotations
 
@@ -36,3 +40,25 @@ def install() -> None:
 def uninstall() -> None:
     for ref_name in MODULES:
         sys.modules.pop(ref_name, None)
+
+
+FOCUS_HELPERS = {"_focus_importance": "focus_importance", "_focus_select": "focus_select"}
+
+
+def patch_modeling(modeling) -> dict:
+    """Swap the FOCUS helpers of a loaded modeling module
+    (``_focus_importance``, ``_focus_select``) for the fdl kernels; returns
+    the replaced functions so ``unpatch_modeling`` can restore them."""
+    from . import focus
+
+    old = {}
+    for name, ours in FOCUS_HELPERS.items():
+        if hasattr(modeling, name):
+            old[name] = getattr(modeling, name)
+            setattr(modeling, name, getattr(focus, ours))
+    return old
+
+
+def unpatch_modeling(modeling, old: dict) -> None:
+    for name, fn in old.items():
+        setattr(modeling, name, fn)

@@ -117,3 +117,30 @@ def test_compaction_index_checks_run_on_the_host():
     bsc = torch.ones(3, 5, 2)
     g2 = regrow(bsc[:, :2], 5, dim=1)
     assert g2.shape == (3, 5, 2) and g2.data_ptr() == bsc.data_ptr() and int(bsc.sum()) == 0
+
+
+def test_module_aliasing_and_modeling_patch():
+    """install() makes the reference's hot-path module names resolve to this
+    package; patch_modeling() swaps the FOCUS helpers by name and restores them."""
+    import importlib
+    import sys
+    import types
+
+    from fast_v2_b200 import dropin, focus
+    from fast_v2_b200.utils import static_kv_cache as ours
+
+    dropin.install()
+    try:
+        mod = importlib.import_module("utils.static_kv_cache")
+        assert mod is ours and mod.StaticKVCache is ours.StaticKVCache
+        assert sys.modules["fused_sparse_extension"].fused_gather_input_rmsnorm_pair is not None
+    finally:
+        dropin.uninstall()
+    assert "utils.static_kv_cache" not in sys.modules
+    modeling = types.ModuleType("fake_modeling")
+    modeling._focus_select = orig_sel = lambda *a, **k: None
+    modeling._focus_importance = orig_imp = lambda *a, **k: None
+    old = dropin.patch_modeling(modeling)
+    assert modeling._focus_select is focus.focus_select and modeling._focus_importance is focus.focus_importance
+    dropin.unpatch_modeling(modeling, old)
+    assert modeling._focus_select is orig_sel and modeling._focus_importance is orig_imp
