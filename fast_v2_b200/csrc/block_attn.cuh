@@ -414,10 +414,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         ptx::tc_fence_after();
         if (pad_warp) {
           __syncwarp();
-          if (lane == 0) {
-            ptx::mbar_arrive(&bars->s_free[buf]);
-            ptx::mbar_arrive(&bars->p_full[0]);
+          if (lane == 0) ptx::mbar_arrive(&bars->s_free[buf]);
+          // S(j+1) may be ready long before the other warps finish P(j), so a
+          // padding warp takes its p_full turn for tile j only after
+          // P(j-1) * V_(j-1) has completed -- i.e. after every warp arrived
+          // for tile j-1.  Arriving earlier could complete phase j with this
+          // warp's arrivals for j and j+1 (an early P * V, then phases out of
+          // step).
+          if (j > 0) {
+            ok = __all_sync(0xffffffffu,
+                            ptx::mbar_wait(&bars->pv_done[0], (j - 1) & 1, abort, kWaitTimeoutNs, 10));
+            if (!ok) break;
           }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&bars->p_full[0]);
           continue;
         }
         const uint32_t t_sb = tmem + lane_off + kTmemS + buf * kBlockN;
