@@ -105,6 +105,12 @@ struct AttnBarriers {
   int abort;
 };
 static_assert(sizeof(AttnBarriers) <= 256, "barrier block");
+static_assert(kSmemBytes <= 227 * 1024, "dynamic shared memory beyond the per-CTA limit");
+static_assert(kTmemS + 2 * kBlockN <= kTmemO && kTmemO + 2 * kHeadDim <= kTmemCols, "TMEM: S_0, S_1, O_0, O_1");
+static_assert(kTmemP1 + kBlockN / 2 <= kTmemCols, "TMEM: P of the one-row-tile pipeline");
+static_assert(kAttnWarps == 2 + 2 * 4, "producer, MMA issuer, 4 softmax warps per row tile");
+static_assert(kSmemQ % 1024 == 0 && kSmemK % 1024 == 0 && kSmemV % 1024 == 0 && kKVTile % 1024 == 0,
+              "128-byte swizzle atoms need 1024-byte aligned tiles");
 
 struct TileInfo {
   int src;    // 0 = cache, 1 = appended block
