@@ -195,6 +195,12 @@ def gen(seed):
     return torch.Generator(device="cpu").manual_seed(seed)
 
 
+def dgen(seed):
+    """Seeded generator on the GPU: multi-GB synthetic inputs in milliseconds
+    (the same values on every B200 for a given seed)."""
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
 def wl_gather_norm(args, rank, world, kt: KernelTimer):
     import numpy as np
 
@@ -204,7 +210,8 @@ def wl_gather_norm(args, rank, world, kt: KernelTimer):
     B, S, H, T = 4, 2048, 3584, 512
     nbuf = max(2, math.ceil(3 * L2_BYTES / (B * S * H * 2)))
     g = gen(1000 + rank)
-    xs = [torch.randn(B, S, H, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
+    dg = dgen(1000 + rank)
+    xs = [torch.randn(B, S, H, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(nbuf)]
     idx = torch.stack([torch.sort(torch.randperm(S, generator=g)[:T]).values for _ in range(B)]).cuda()
     w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda()
     outs = [(torch.empty(B, T, H, dtype=torch.bfloat16, device="cuda"),
@@ -248,7 +255,7 @@ def wl_gather_norm(args, rank, world, kt: KernelTimer):
         hxf = xs[0][:1].cpu()
         t0 = time.perf_counter()
         n = 0
-        while time.perf_counter() - t0 < 8.0 or n < 2:
+        while time.perf_counter() - t0 < args.cpu_seconds or n < 2:
             torch_port.gather_input_rmsnorm(hxf, hidx[:1], w.cpu(), 1e-6)
             n += 1
         dt = (time.perf_counter() - t0) / n
@@ -272,10 +279,11 @@ def wl_kv_path(args, rank, world, kt: KernelTimer):
     L, B, S, Hkv, D, rep, n = 28, 16, 4096, 4, 128, args.kv_rep, 32
     g = gen(2000 + rank)
     lens = torch.randint(256, 2049, (B,), generator=g, dtype=torch.int32)
-    kc = [torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
-    vc = [torch.randn(B, S, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
-    kn = [torch.randn(B, n, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
-    vn = [torch.randn(B, n, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(L)]
+    dg = dgen(2001 + rank)
+    kc = [torch.randn(B, S, Hkv, D, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(L)]
+    vc = [torch.randn(B, S, Hkv, D, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(L)]
+    kn = [torch.randn(B, n, Hkv, D, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(L)]
+    vn = [torch.randn(B, n, Hkv, D, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(L)]
     dlens = lens.cuda()
     lens_after = (lens + n).cuda()
     cu = torch.zeros(B + 1, dtype=torch.int32)
@@ -329,12 +337,12 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
     ensure_ops()
     B, P, Sq, Hq, Hkv, D = args.attn_b, args.attn_p, args.attn_sq, args.attn_hq, args.attn_hkv, 128
     cap = P + 32
-    g = gen(3000 + rank)
+    g = dgen(3000 + rank)
     kv_bytes = B * cap * Hkv * D * 2 * 2
     nbuf = max(1, math.ceil(3 * L2_BYTES / kv_bytes)) if kv_bytes < 3 * L2_BYTES else 1
-    ks = [torch.randn(B, cap, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
-    vs = [torch.randn(B, cap, Hkv, D, generator=g).to(torch.bfloat16).cuda() for _ in range(nbuf)]
-    q = (torch.randn(B, Sq, Hq, D, generator=g) / math.sqrt(D)).to(torch.bfloat16).cuda()
+    ks = [torch.randn(B, cap, Hkv, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(nbuf)]
+    vs = [torch.randn(B, cap, Hkv, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(nbuf)]
+    q = (torch.randn(B, Sq, Hq, D, generator=g, device="cuda") / math.sqrt(D)).to(torch.bfloat16)
     seq = torch.full((B,), cap, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
     splits = args.attn_splits or _lib.attn_auto_splits(B, Sq, Hq, Hkv, cap, 0)
@@ -356,7 +364,7 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
         hq, hk, hv = q[:bb].cpu(), ks[0][:bb].cpu(), vs[0][:bb].cpu()
         t0 = time.perf_counter()
         nrep = 0
-        while time.perf_counter() - t0 < 8.0 or nrep < 1:
+        while time.perf_counter() - t0 < args.cpu_seconds or nrep < 1:
             torch_port.flash_kvcache_sdpa(hq, hk, hv, seq[:bb].cpu(), D ** -0.5)
             nrep += 1
         dt = (time.perf_counter() - t0) / nrep
@@ -405,7 +413,8 @@ def _e2e(args, rank, world, kt, geo_name):
     # spare); G (the configured generation length) is the minimum.
     G = max(G, 32 * (args.warmup + args.steps + 2))
     cpu_only = getattr(args, "impl", "ours") == "reference"
-    model = None if cpu_only else BlockDiffusionLM(geo, device="cuda", seed=100 + rank)
+    # One weight replica per rank: every rank builds the same seeded weights.
+    model = None if cpu_only else BlockDiffusionLM(geo, device="cuda", seed=100)
     if model is not None:
         # Random weights can put the mask token on top of the argmax, which a
         # trained model never does (and which stalls the reference's unmask
@@ -425,12 +434,18 @@ def _e2e(args, rank, world, kt, geo_name):
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
                                                       fed_bucket=getattr(args, "fed_bucket", 1), use_graphs=True)
-    g = gen(4000 + rank)
     if not cpu_only:
-        prompt = torch.randint(0, 151643, (B, P), generator=g).cuda()
+        # One seeded global batch of B x world prompts; each rank decodes its
+        # own contiguous shard of sequences (sequence_shard), as the
+        # reference's request-level data parallelism does.
+        from fast_v2_b200.sharding import sequence_shard
+
+        all_prompts = torch.randint(0, 151643, (B * world, P), generator=gen(4000))
+        first, n_local = sequence_shard(B * world, world, rank)
+        prompt = all_prompts[first:first + n_local].cuda()
         max_blocks = G // 32
         with torch.no_grad():
-            state = {"bridge": dec.prefill(prompt), "blocks": 0}
+            state = {"bridge": dec.prefill(prompt), "blocks": 0, "gen": []}
             dec.capture_all()
         torch.cuda.synchronize()
         stats = {}
@@ -438,6 +453,7 @@ def _e2e(args, rank, world, kt, geo_name):
         def step():
             with torch.no_grad():
                 state["blk"], state["bridge"] = dec.decode_block(state["bridge"], stats=stats)
+            state["gen"].append(state["blk"])
             state["blocks"] += 1
 
         def reserve(n):
@@ -447,7 +463,13 @@ def _e2e(args, rank, world, kt, geo_name):
                 with torch.no_grad():
                     state["bridge"] = dec.prefill(prompt)
                 state["blocks"] = 0
+                state["gen"] = []
                 torch.cuda.synchronize()
+
+        def collect():
+            """This rank's generated sequences since the last prefill: prompt
+            followed by every decoded 32-token block."""
+            return torch.cat([prompt] + state["gen"], dim=1)
 
         # e2e: the host-facing call per block -- bridge token in from pinned host
         # memory, the block's 32 tokens back to pinned host memory.
@@ -461,6 +483,7 @@ def _e2e(args, rank, world, kt, geo_name):
                 state["blk"], state["bridge"] = dec.decode_block(bridge, stats=stats)
                 hblk.copy_(state["blk"], non_blocking=True)
             torch.cuda.current_stream().synchronize()
+            state["gen"].append(state["blk"])
             state["blocks"] += 1
 
         # dominant kernel of ours in the step: the block attention of a full
@@ -519,7 +542,7 @@ def _e2e(args, rank, world, kt, geo_name):
         return dict(meta, cpu_sample=cpu_sample)
     kvb, fl = dom_work()
     return dict(meta, units_per_step=B * 32, step=step, dominant=dominant, graph=False, e2e_step=e2e_step,
-                collect=lambda: state["blk"], reserve=reserve,
+                collect=collect, reserve=reserve,
                 e2e_bytes=(B * 8, B * 32 * 8),
                 roofline=dict(bound="hbm", per_launch=kvb, kernel="block_attn_kernel (full dKV step, layer 0)",
                               flops=fl, dynamic=dom_work),
@@ -564,6 +587,92 @@ def wl_compact(args, rank, world, kt: KernelTimer):
         dtype="bf16", cpu_sample=cpu_sample)
 
 
+def wl_swiglu(args, rank, world, kt: KernelTimer):
+    """SwiGLU of the 7B MLP at a full dKV step of the e2e bench: gate/up rows
+    [64 x 32, 2 x 18944] bf16 -> [2048, 18944] (silu(gate) * up, the
+    reference's bf16 roundings)."""
+    from fast_v2_b200 import ensure_ops
+
+    ensure_ops()
+    rows, F = 64 * 32, 18944
+    dg = dgen(6000 + rank)
+    per = rows * 3 * F * 2
+    nbuf = max(2, math.ceil(3 * L2_BYTES / per))
+    gus = [(torch.randn(rows, 2 * F, generator=dg, device="cuda") * 2).to(torch.bfloat16) for _ in range(nbuf)]
+    outs = [torch.empty(rows, F, dtype=torch.bfloat16, device="cuda") for _ in range(nbuf)]
+    alg = rows * F * 2 * 3  # read gate + up, write the product
+    state = {"i": 0}
+
+    def step():
+        i = state["i"] % nbuf
+        state["i"] += 1
+        torch.ops.fdl.swiglu(gus[i], outs[i])
+
+    def cpu_sample():
+        from oracle import torch_port
+
+        h = gus[0][:64].cpu()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < args.cpu_seconds or n < 2:
+            torch_port.swiglu(h)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return alg / rows * 64 / dt / 1e9, f"{n} calls on 64 of {rows} rows (silu(gate) * up in bf16 torch)"
+
+    return dict(
+        metric="SwiGLU throughput (algorithmic HBM GB/s)", unit="GB/s", units_per_step=alg / 1e9, step=step,
+        dominant=step, graph=True, e2e_step=None, e2e_bytes=None,
+        roofline=dict(bound="hbm", per_launch=alg, kernel="swiglu_kernel"), launches_per_step=1,
+        config={"workload": "swiglu", "rows": rows, "ffn": F, "shape": "7B MLP, full dKV step of 64 sequences",
+                "l2": f"inputs rotate over {nbuf} buffer sets"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
+def wl_add_rmsnorm(args, rank, world, kt: KernelTimer):
+    """Residual add + RMSNorm of the 7B decoder layer at a full dKV step:
+    h += y (bf16) and normed = RMSNorm(h) * w over [2048, 3584] rows."""
+    from fast_v2_b200 import ensure_ops
+
+    ensure_ops()
+    rows, H = 64 * 32, 3584
+    dg = dgen(6100 + rank)
+    per = rows * H * 2 * 4
+    nbuf = max(2, math.ceil(3 * L2_BYTES / per))
+    ys = [torch.randn(rows, H, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(nbuf)]
+    hs = [torch.randn(rows, H, generator=dg, device="cuda").to(torch.bfloat16) for _ in range(nbuf)]
+    outs = [torch.empty(rows, H, dtype=torch.bfloat16, device="cuda") for _ in range(nbuf)]
+    w = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    alg = rows * H * 2 * 4  # read y and h; write h and normed
+    state = {"i": 0}
+
+    def step():
+        i = state["i"] % nbuf
+        state["i"] += 1
+        torch.ops.fdl.add_rmsnorm(ys[i], hs[i], w, 1e-6, hs[i], outs[i])
+
+    def cpu_sample():
+        from oracle import torch_port
+
+        y, h, wc = ys[0][:64].cpu(), hs[0][:64].cpu(), w.cpu()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < args.cpu_seconds or n < 2:
+            torch_port.rmsnorm(h + y, wc, 1e-6)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return alg / rows * 64 / dt / 1e9, f"{n} calls on 64 of {rows} rows (residual add + Qwen RMSNorm in torch)"
+
+    return dict(
+        metric="residual add + RMSNorm throughput (algorithmic HBM GB/s)", unit="GB/s", units_per_step=alg / 1e9,
+        step=step, dominant=step, graph=True, e2e_step=None, e2e_bytes=None,
+        roofline=dict(bound="hbm", per_launch=alg, kernel="gather_rmsnorm_kernel (residual form)"),
+        launches_per_step=1,
+        config={"workload": "add_rmsnorm", "rows": rows, "hidden": H, "shape": "7B layer, full dKV step of 64 sequences",
+                "l2": f"inputs rotate over {nbuf} buffer sets"},
+        dtype="bf16", cpu_sample=cpu_sample)
+
+
 def wl_e2e_7b(args, rank, world, kt):
     return _e2e(args, rank, world, kt, "7b")
 
@@ -573,7 +682,7 @@ def wl_e2e_1_5b(args, rank, world, kt):
 
 
 WORKLOADS = {"gather_norm": wl_gather_norm, "kv_path": wl_kv_path, "block_attn": wl_block_attn, "compact": wl_compact,
-             "e2e_7b": wl_e2e_7b, "e2e_1_5b": wl_e2e_1_5b}
+             "swiglu": wl_swiglu, "add_rmsnorm": wl_add_rmsnorm, "e2e_7b": wl_e2e_7b, "e2e_1_5b": wl_e2e_1_5b}
 DEFAULT_CONFIG = "e2e_7b"
 
 
@@ -610,15 +719,207 @@ def run_reference(args, world, rank):
         vals.append(v)
     wall = time.perf_counter() - t_all
     value = statistics.median(vals)
+    # tokens/s samples commit one token per forward of one sequence, so one
+    # step of this arm is one (scaled) forward: 1000 / value ms.  Otherwise a
+    # step is one sample call.
+    ms_step = 1e3 / value if w["unit"] == "tokens/s" else wall / max(1, args.steps) * 1e3
     line = {
         "impl": "reference", "metric": w["metric"], "value": value, "unit": w["unit"], "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / max(1, args.steps) * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"],
         "data": "synthetic", "config": w["config"],
         "cpu_baseline": {"value": value, "unit": w["unit"], "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": w["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
+
+
+# --------------------------------------------------------------------------
+# measurement helpers
+# --------------------------------------------------------------------------
+def timed_region(w, steps, world, stream, sampler=None):
+    """W warm-up steps are the caller's; here: optional CUDA-graph capture of
+    the K steps, then the timed region bracketed by barrier + synchronize,
+    CUDA events on the launching stream.  Returns (max-over-ranks ms, host
+    launch tally inside the region, wall-clock window)."""
+    from fast_v2_b200 import _lib as _fdl_lib
+
+    graph = None
+    if w.get("graph"):
+        # Kernel-level configs: the K steps are replayed from a CUDA graph so
+        # the device time is not diluted by host dispatch gaps.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(steps):
+                w["step"]()
+        graph.replay()
+        barrier(world)
+    if sampler is not None:
+        sampler.start()
+    barrier(world)
+    launches0 = _fdl_lib.launches
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    start.record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for _ in range(steps):
+            w["step"]()
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    launches = _fdl_lib.launches - launches0
+    if sampler is not None:
+        sampler.mark(t0, t1)
+    barrier(world)
+    if sampler is not None:
+        sampler.stop()
+    del graph
+    return max_over_ranks(start.elapsed_time(end), world), launches, (t0, t1)
+
+
+def launch_ms(fn, n, stream):
+    """Mean duration of fn's own launches: n of them back to back in a CUDA
+    graph, CUDA events on the launching stream."""
+    gd = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gd):
+        for _ in range(n):
+            fn()
+    gd.replay()
+    torch.cuda.synchronize()
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s1.record(stream)
+    gd.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del gd
+    return s1.elapsed_time(e1) / n
+
+
+def roofline_of(rf, kms, peaks, traffic_key=None):
+    if not kms:
+        return None
+    if rf["bound"] == "hbm":
+        ach = rf["per_launch"] / (kms / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": None, "kernel": rf["kernel"], "launch_us": round(kms * 1e3, 2),
+                "alg_bytes_per_launch": int(rf["per_launch"]), "peak_src": peaks["src"]}
+        if rf.get("flops"):
+            roof["tflops_achieved"] = round(rf["flops"] / (kms / 1e3) / 1e12, 1)
+    else:
+        ach = rf["per_launch"] / (kms / 1e3) / 1e12
+        peak = peaks["bf16_tflops"]
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"], "launch_us": round(kms * 1e3, 2),
+                "alg_flops_per_launch": int(rf["per_launch"]), "peak_src": peaks["src"]}
+        if rf.get("hbm_bytes"):
+            roof["hbm_gbs_achieved"] = round(rf["hbm_bytes"] / (kms / 1e3) / 1e9, 1)
+            roof["hbm_frac"] = round(rf["hbm_bytes"] / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)
+    tr = ROOT / "profiles" / "traffic.json"
+    if traffic_key and tr.exists():
+        t = json.loads(tr.read_text()).get(traffic_key)
+        if t:
+            roof["traffic"] = t
+    return roof
+
+
+def kernel_breakdown(fn):
+    """Device time per kernel name over one call of fn (one untimed decode
+    block), from a CUDA activity trace (torch.profiler / CUPTI).  This is an
+    attribution of the step's device time to kernels, not a bench value.
+    Returns [(name, launches, total_ms)] sorted by time, or None."""
+    try:
+        from torch.autograd import DeviceType
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        agg = {}
+        for e in prof.events():
+            if getattr(e, "device_type", None) != DeviceType.CUDA:
+                continue
+            name = e.name
+            if name.startswith("Memcpy") or name.startswith("Memset"):
+                continue
+            dur = e.time_range.elapsed_us() / 1e3
+            n, t = agg.get(name, (0, 0.0))
+            agg[name] = (n + 1, t + dur)
+        rows = sorted(((k, n, t) for k, (n, t) in agg.items()), key=lambda r: -r[2])
+        return rows or None
+    except Exception as ex:  # the trace is optional evidence; never fail the bench on it
+        sys.stderr.write(f"kernel breakdown unavailable: {ex}\n")
+        return None
+
+
+def short_kernel_name(name: str) -> str:
+    n = name
+    for pre in ("void ",):
+        if n.startswith(pre):
+            n = n[len(pre):]
+    return n.split("(")[0][:90]
+
+
+# Kernel-level configs measured inside the default run (BASELINE configs 1-3
+# and the two largest kernels of ours in the e2e step), each on its own
+# inputs, after the headline's timed region.
+KERNEL_SUITE = [
+    ("gather_norm", {}, 400),
+    ("kv_path", {}, 20),
+    ("block_attn", {"attn_b": 64, "attn_p": 8192, "attn_sq": 32}, 40),
+    ("block_attn", {"attn_b": 16, "attn_p": 8192, "attn_sq": 32}, 100),
+    ("block_attn", {"attn_b": 16, "attn_p": 4096, "attn_sq": 32}, 150),
+    ("block_attn", {"attn_b": 64, "attn_p": 8192, "attn_sq": 8}, 100),
+    ("swiglu", {}, 200),
+    ("add_rmsnorm", {}, 400),
+]
+
+
+def run_kernel_suite(args, rank, world, peaks, stream):
+    import copy
+    import gc
+
+    out = {}
+    for name, over, steps in KERNEL_SUITE:
+        a = copy.copy(args)
+        for k2, v2 in over.items():
+            setattr(a, k2, v2)
+        a.cpu_seconds = 2.0
+        w = WORKLOADS[name](a, rank, world, KernelTimer())
+        for _ in range(3):
+            w["step"]()
+        torch.cuda.synchronize()
+        ms, _, _ = timed_region(w, steps, world, stream)
+        value = w["units_per_step"] * steps * world / (ms / 1e3)
+        kms = launch_ms(w["dominant"], max(20, min(200, steps)), stream)
+        key = name if not over else f"{name}_b{a.attn_b}_p{a.attn_p}_sq{a.attn_sq}"
+        cpu = None
+        if rank == 0 and not args.no_cpu_baseline:
+            v, sample = w["cpu_sample"]()
+            cpu = {"value": v, "unit": w["unit"], "cores": torch.get_num_threads(), "kind": "port", "sample": sample}
+        out[key] = {"metric": w["metric"], "value": value, "unit": w["unit"], "steps": steps,
+                    "ms_per_step": ms / steps, "roofline": roofline_of(w["roofline"], kms, peaks, key),
+                    "config": w["config"], "cpu_baseline": cpu}
+        w.clear()
+        del w
+        gc.collect()
+        torch.cuda.empty_cache()
+    return out
+
+
+def e2e_dominant(breakdown, geo_B=64):
+    """The largest kernel of ours in the e2e step by device time, with a
+    standalone workload of the same launch shape to time it."""
+    cands = {"swiglu_kernel": "swiglu", "gather_rmsnorm_kernel": "add_rmsnorm", "block_attn_kernel": None}
+    if breakdown:
+        for nm, _, _ in breakdown:
+            for c, wl in cands.items():
+                if c in nm:
+                    return c, wl
+    return "swiglu_kernel", "swiglu"
 
 
 # --------------------------------------------------------------------------
@@ -641,9 +942,13 @@ def main():
     ap.add_argument("--fed-bucket", type=int, default=1,
                     help="cached dKV steps run at the fed width rounded up to this multiple (1 = exact, as the reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="e2e configs at N=1: skip the kernel-level measurements added to the line")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="length of each CPU-baseline sample")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"gather_norm": 2000, "kv_path": 100, "block_attn": 200}.get(args.config, 8)
+        args.steps = {"gather_norm": 2000, "kv_path": 100, "block_attn": 200, "swiglu": 500,
+                      "add_rmsnorm": 1000}.get(args.config, 8)
     args.warmup = max(3, args.warmup)
     world, rank, local = setup_dist()
 
@@ -655,96 +960,23 @@ def main():
             dist.destroy_process_group()
         return
 
+    from fast_v2_b200 import _lib as _fdl_lib
+
     peaks = load_peaks()
     kt = KernelTimer()
     w = WORKLOADS[args.config](args, rank, world, kt)
+    meta = {k: w[k] for k in ("metric", "unit", "config", "launches_per_step", "dtype")}
     for _ in range(args.warmup):
         w["step"]()
     barrier(world)
+    _fdl_lib.check_device("bench warm-up")
     stream = torch.cuda.current_stream()
-    graph = None
-    if w.get("graph"):
-        # Kernel-level configs: the K steps are replayed from a CUDA graph so
-        # the device time is not diluted by host dispatch gaps.
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for _ in range(args.steps):
-                w["step"]()
-        graph.replay()
-        barrier(world)
     sampler = ClockSampler(local)
-    sampler.start()
-    barrier(world)
     kt.active = not w.get("graph")
-    from fast_v2_b200 import _lib as _fdl_lib
-    launches0 = _fdl_lib.launches
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.time()
-    start.record(stream)
-    if graph is not None:
-        graph.replay()
-    else:
-        for _ in range(args.steps):
-            w["step"]()
-    end.record(stream)
-    torch.cuda.synchronize()
-    t1 = time.time()
+    ms_max, launches_timed, _ = timed_region(w, args.steps, world, stream, sampler)
     kt.active = False
-    launches_timed = _fdl_lib.launches - launches0
-    sampler.mark(t0, t1)
-    barrier(world)
-    sampler.stop()
-    ms = start.elapsed_time(end)
-    ms_max = max_over_ranks(ms, world)
+    _fdl_lib.check_device("bench timed region")
     value = w["units_per_step"] * args.steps * world / (ms_max / 1e3)
-    del graph
-
-    # dominant-kernel duration: its own launches back to back in a CUDA graph,
-    # timed with events on the launching stream.
-    rf = w["roofline"]
-    kms = None
-    if w.get("dominant") is not None:
-        n_dom = max(20, min(500, args.steps))
-        gd = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gd):
-            for _ in range(n_dom):
-                w["dominant"]()
-        gd.replay()
-        torch.cuda.synchronize()
-        s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s1.record(stream)
-        gd.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        kms = s1.elapsed_time(e1) / n_dom
-        del gd
-    else:
-        kms = kt.avg_ms()
-    roof = None
-    if rf.get("dynamic"):
-        rf["per_launch"], rf["flops"] = rf["dynamic"]()
-    if kms:
-        if rf["bound"] == "hbm":
-            ach = rf["per_launch"] / (kms / 1e3) / 1e9
-            peak = peaks["hbm_gbs"]
-            roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"],
-                    "launch_us": round(kms * 1e3, 2), "peak_src": peaks["src"]}
-            if rf.get("flops"):
-                roof["tflops_achieved"] = round(rf["flops"] / (kms / 1e3) / 1e12, 1)
-        else:
-            ach = rf["per_launch"] / (kms / 1e3) / 1e12
-            peak = peaks["bf16_tflops"]
-            roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
-                    "frac": round(ach / peak, 4), "traffic": None, "kernel": rf["kernel"],
-                    "launch_us": round(kms * 1e3, 2), "peak_src": peaks["src"]}
-            if rf.get("hbm_bytes"):
-                roof["hbm_gbs_achieved"] = round(rf["hbm_bytes"] / (kms / 1e3) / 1e9, 1)
-        tr = ROOT / "profiles" / "traffic.json"
-        if tr.exists():
-            t = json.loads(tr.read_text()).get(args.config)
-            if t:
-                roof["traffic"] = t
 
     # end-to-end through the public API with host buffers
     e2e = None
@@ -764,10 +996,64 @@ def main():
         ms2 = max_over_ranks(s2.elapsed_time(e2), world)
         e2e = {"value": w["units_per_step"] * n_e2e * world / (ms2 / 1e3), "unit": w["unit"],
                "h2d_bytes_per_step": w["e2e_bytes"][0], "d2h_bytes_per_step": w["e2e_bytes"][1]}
+        _fdl_lib.check_device("bench end-to-end region")
 
-    # Sequence-sharded output: one all-gather of every rank's last generated
-    # block after the timed regions (the only collective besides the max-time
-    # reduction).
+    # Roofline of the dominant kernel.  Kernel-level configs: the config's own
+    # kernel.  e2e configs: the largest kernel of this library in the step by
+    # device time (attribution from one untimed, traced block), timed alone at
+    # the step's full-block launch shape.
+    rf = w["roofline"]
+    breakdown = None
+    dom_shares = None
+    if w.get("stats") is not None and w.get("e2e_step"):
+        if w.get("reserve"):
+            w["reserve"](2)
+        breakdown = kernel_breakdown(w["step"])
+        if breakdown:
+            total = sum(t for _, _, t in breakdown)
+            ours = [(short_kernel_name(n), c, t) for n, c, t in breakdown if "fdl::" in n]
+            dom_shares = {"source": "one untimed decode block, CUDA activity trace (torch.profiler)",
+                          "device_ms": round(total, 2),
+                          "fdl_share": round(sum(t for _, _, t in ours) / total, 4),
+                          "fdl_kernels": [{"kernel": n, "launches": c, "ms": round(t, 3), "share": round(t / total, 4)}
+                                          for n, c, t in ours[:8]],
+                          "top_kernels": [{"kernel": short_kernel_name(n), "launches": c, "ms": round(t, 3),
+                                           "share": round(t / total, 4)} for n, c, t in breakdown[:6]]}
+    traffic_key = args.config
+    kname = None
+    if w.get("stats") is not None:
+        kname, wl_name = e2e_dominant(breakdown)
+        if wl_name is not None:
+            import copy
+
+            a2 = copy.copy(args)
+            a2.cpu_seconds = 1.0
+            wd = WORKLOADS[wl_name](a2, rank, world, KernelTimer())
+            kms = launch_ms(wd["dominant"], 200, stream)
+            rf = dict(wd["roofline"])
+            rf["kernel"] = f"{kname} at the e2e full-block launch shape ({wd['config']['rows']} rows)"
+            traffic_key = wl_name
+            wd.clear()
+        else:
+            if rf.get("dynamic"):
+                rf["per_launch"], rf["flops"] = rf["dynamic"]()
+            kms = launch_ms(w["dominant"], 200, stream)
+            traffic_key = None
+    elif w.get("dominant") is not None:
+        kms = launch_ms(w["dominant"], max(20, min(500, args.steps)), stream)
+    else:
+        kms = kt.avg_ms()
+    roof = roofline_of(rf, kms, peaks, traffic_key)
+    if roof is not None and dom_shares is not None:
+        for k in dom_shares["fdl_kernels"]:
+            if kname in k["kernel"]:
+                roof["share_of_step"] = k["share"]
+                break
+        roof["step_breakdown"] = dom_shares
+
+    # Sequence-sharded output: one all-gather of every rank's generated
+    # sequences after the timed regions (the only collective besides the
+    # max-time reduction).
     collected = None
     if world > 1 and w.get("collect"):
         from fast_v2_b200.sharding import gather_generated
@@ -779,18 +1065,34 @@ def main():
         torch.set_num_threads(os.cpu_count() or 1)
         v, sample = w["cpu_sample"]()
         cpu = {"value": v, "unit": w["unit"], "cores": torch.get_num_threads(), "kind": "port", "sample": sample}
+    clocks = sampler.summary()
+
+    kernels = None
+    if world == 1 and w.get("stats") is not None and not args.no_kernels:
+        import gc
+
+        w.clear()
+        del w
+        gc.collect()
+        torch.cuda.empty_cache()
+        kernels = run_kernel_suite(args, rank, world, peaks, stream)
+        w = {}
+    _fdl_lib.check_device("bench kernel measurements")
 
     if rank == 0:
         line = {
-            "metric": w["metric"], "value": value, "unit": w["unit"], "n_gpus": world, "steps": args.steps,
+            "metric": meta["metric"], "value": value, "unit": meta["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-            "config": {**w["config"], "parallelism": f"dp{world} (sequence-sharded replicas)",
-                       **({"gathered_block": collected} if collected else {})},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": sampler.summary(),
-            "gpu_launches": (w["launches_per_step"] * args.steps if w["launches_per_step"] is not None
-                             else launches_timed),
+            "scaling": "weak", "vs_baseline": None, "dtype": meta["dtype"], "data": "synthetic",
+            "config": {**meta["config"], "parallelism": f"dp{world} (sequence-sharded replicas)",
+                       **({"gathered": collected} if collected else {})},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": (meta["launches_per_step"] * args.steps
+                             if meta["launches_per_step"] is not None else launches_timed),
+            "device_status": 0,
         }
+        if kernels is not None:
+            line["kernels"] = kernels
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -119,6 +119,28 @@ def last_device_error() -> tuple[int, int]:
     return int(code.value), int(info.value)
 
 
+class DeviceError(RuntimeError):
+    """A kernel of the library recorded a device-side error (an index or
+    length outside its buffer, or a pipeline wait that gave up)."""
+
+    def __init__(self, where: str, code: int, info: int):
+        self.code, self.info = code, info
+        super().__init__(f"{where}: device status {DEVICE_CODES.get(code, code)} (info {info})")
+
+
+DEVICE_CODES = {1: "FDL_DEV_INDEX: a position or index outside its buffer (the row was skipped)",
+                2: "FDL_DEV_LENGTH: a per-sequence length outside [0, capacity] (clamped)",
+                3: "FDL_DEV_TIMEOUT: a pipeline wait gave up; the attention output is incomplete"}
+
+
+def check_device(where: str) -> None:
+    """Raise DeviceError if any kernel recorded a device-side error since the
+    last check (synchronises the current device and clears the status)."""
+    code, info = last_device_error()
+    if code != 0:
+        raise DeviceError(where, code, info)
+
+
 def sparse_prefix_workspace_bytes(batch: int, cap: int) -> int:
     return int(abi().fdl_sparse_prefix_workspace_bytes(batch, cap))
 

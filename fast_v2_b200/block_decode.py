@@ -462,7 +462,7 @@ class BlockDiffusionDecoder:
         for key in ["begin", "full", "commit"] + list(range(self.fed_bucket, self.block + 1, self.fed_bucket)):
             if key not in self._graphs:
                 self._capture(key)
-        torch.cuda.synchronize()
+        _lib.check_device("BlockDiffusionDecoder.capture_all")
 
     def _run(self, key):
         if not self.use_graphs:
@@ -480,7 +480,9 @@ class BlockDiffusionDecoder:
         self.st.lens.zero_()
         self.finished.zero_()
         hl = self.st.forward_commit(prompt, pos)
-        return self.m.logits_rows(hl).argmax(-1, keepdim=True)
+        bridge = self.m.logits_rows(hl).argmax(-1, keepdim=True)
+        _lib.check_device("BlockDiffusionDecoder.prefill")
+        return bridge
 
     def decode_block(self, bridge: torch.Tensor, stats: dict | None = None):
         """Decode one block: [bridge token, 31 masks] -> 32 tokens; commit;
@@ -510,12 +512,16 @@ class BlockDiffusionDecoder:
                 step_in_block += 1
                 # One device-to-host read per step: the step's own status.
                 self.status_h.copy_(self.status, non_blocking=True)
-                torch.cuda.current_stream(self.status.device).synchronize()
+                if self.status.is_cuda:
+                    torch.cuda.current_stream(self.status.device).synchronize()
                 more, fed_n = bool(self.status_h[0]), int(self.status_h[1])
         x = self.x.clone()
         self._run("commit")
         n_fwd += 1
         nxt = self.nxt.clone()
+        # Once per block: any kernel that skipped a row or gave up a wait
+        # stops the decode here instead of letting it continue on bad K/V.
+        _lib.check_device("BlockDiffusionDecoder.decode_block")
         if stats is not None:
             stats["forwards"] = stats.get("forwards", 0) + n_fwd
             stats["blocks"] = stats.get("blocks", 0) + 1

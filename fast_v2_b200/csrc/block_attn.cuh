@@ -64,7 +64,7 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 #ifndef FDL_ATTN_PREFETCH
 #define FDL_ATTN_PREFETCH 1
 #endif
-constexpr int kPrefetch = FDL_ATTN_PREFETCH;  // key tiles prefetched into L2 ahead of the smem ring  // of every 8 exponential pairs, on the FMA pipe
+constexpr int kPrefetch = FDL_ATTN_PREFETCH;  // key tiles prefetched into L2 ahead of the smem ring
 
 constexpr uint32_t kSmemQ = 0;                        // 2 halves x 256 rows x 128 B
 constexpr uint32_t kQHalf = 256 * 128;                // 32 KB
@@ -107,7 +107,11 @@ struct AttnBarriers {
 static_assert(sizeof(AttnBarriers) <= 256, "barrier block");
 static_assert(kSmemBytes <= 227 * 1024, "dynamic shared memory beyond the per-CTA limit");
 static_assert(kTmemS + 2 * kBlockN <= kTmemO && kTmemO + 2 * kHeadDim <= kTmemCols, "TMEM: S_0, S_1, O_0, O_1");
+// The one-row-tile pipeline's P sits in the columns of O_1 on purpose: with a
+// single row tile O_1 is unused.  It must not reach into either S buffer or O_0.
 static_assert(kTmemP1 + kBlockN / 2 <= kTmemCols, "TMEM: P of the one-row-tile pipeline");
+static_assert(kTmemP1 >= kTmemO + kHeadDim, "TMEM: P of the one-row-tile pipeline overlaps O_0");
+static_assert(kTmemP1 >= kTmemS + 2 * kBlockN, "TMEM: P of the one-row-tile pipeline overlaps an S buffer");
 static_assert(kAttnWarps == 2 + 2 * 4, "producer, MMA issuer, 4 softmax warps per row tile");
 static_assert(kSmemQ % 1024 == 0 && kSmemK % 1024 == 0 && kSmemV % 1024 == 0 && kKVTile % 1024 == 0,
               "128-byte swizzle atoms need 1024-byte aligned tiles");

@@ -171,7 +171,8 @@ int fdl_kv_scatter(void* k_dst, void* v_dst, const void* k_src, const void* v_sr
 
 int fdl_kv_gather_prefix(const void* k_prefix, const void* v_prefix, const int32_t* len, int prefix_cap,
                          const void* k_block, const void* v_block, int n_blk, void* k_out, void* v_out,
-                         const int32_t* cu_seqlens, int batch, int heads, int head_dim, int rep, int elem_bytes,
+                         const int32_t* cu_seqlens, int64_t out_rows, int batch, int heads, int head_dim, int rep,
+                         int elem_bytes,
                          int64_t pre_sb, int64_t pre_ss, int64_t pre_sh, int64_t blk_sb, int64_t blk_ss,
                          int64_t blk_sh, int64_t out_sb, int64_t out_ss, int64_t out_sh, fdl_stream_t stream) {
   if (batch < 1 || batch > 65535 || prefix_cap < 0 || n_blk < 0 || heads < 1 || head_dim < 1 || rep < 1)
@@ -181,6 +182,7 @@ int fdl_kv_gather_prefix(const void* k_prefix, const void* v_prefix, const int32
   if (!len || (!k_out && !v_out)) return FDL_E_NULL;
   if (!k_prefix || !k_out || (v_out && !v_prefix)) return FDL_E_NULL;
   if (n_blk > 0 && (!k_block || (v_out && !v_block))) return FDL_E_NULL;
+  if (cu_seqlens && out_rows < 0) return FDL_E_SHAPE;
   GatherPrefixArgs a{};
   const int64_t rb = static_cast<int64_t>(head_dim) * elem_bytes;
   a.pre[0] = static_cast<const char*>(k_prefix);
@@ -205,6 +207,7 @@ int fdl_kv_gather_prefix(const void* k_prefix, const void* v_prefix, const int32
   if (total == 0) return FDL_OK;
   a.len = len;
   a.cu = cu_seqlens;
+  a.out_rows = out_rows;
   a.prefix_cap = prefix_cap;
   a.n_blk = n_blk;
   a.rep = rep;

@@ -126,6 +126,7 @@ struct GatherPrefixArgs {
   char* out[2];
   const int32_t* len;
   const int32_t* cu;
+  int64_t out_rows;  // rows of the packed output (cu != nullptr)
   int prefix_cap, n_blk, rep;
   uint32_t total;  // (prefix_cap + n_blk) * Hs * vpr
   FastDiv vpr, heads;
@@ -141,6 +142,16 @@ __global__ void __launch_bounds__(kCopyThreads) kv_gather_prefix_kernel(const __
   if (len < 0 || len > a.prefix_cap) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && which == 0) report(FDL_DEV_LENGTH, len);
     len = len < 0 ? 0 : a.prefix_cap;
+  }
+  if (a.cu) {
+    // The packed range of sequence b is [cu[b], cu[b+1]); it must hold the
+    // len + n_blk rows written here and lie inside the output.  A sequence
+    // whose range does not is skipped whole and reported.
+    const int64_t c0 = a.cu[b], c1 = a.cu[b + 1];
+    if (c0 < 0 || c1 > a.out_rows || c0 + len + a.n_blk > c1) {
+      if (threadIdx.x == 0 && blockIdx.x == 0 && which == 0) report(FDL_DEV_INDEX, b);
+      return;
+    }
   }
   const uint32_t per_tok = a.heads.d * a.vpr.d;
   const uint32_t limit = static_cast<uint32_t>(len + a.n_blk) * per_tok;

@@ -196,7 +196,7 @@ void kv_gather_prefix(const Tensor& k_prefix, const Tensor& v_prefix, const Tens
   check_rc(fdl_kv_gather_prefix(k_prefix.data_ptr(), v_prefix.data_ptr(), lens.data_ptr<int32_t>(),
                                 static_cast<int>(p.S), k_block ? k_block->data_ptr() : nullptr,
                                 v_block ? v_block->data_ptr() : nullptr, n_blk, k_out.data_ptr(), v_out.data_ptr(),
-                                cu, static_cast<int>(p.B), static_cast<int>(p.H), static_cast<int>(p.D),
+                                cu, cu ? k_out.size(0) : 0, static_cast<int>(p.B), static_cast<int>(p.H), static_cast<int>(p.D),
                                 static_cast<int>(rep), elem_bytes(k_prefix), p.sb, p.ss, p.sh, bl.sb, bl.ss, bl.sh,
                                 osb, oss, osh, cur_stream()),
            "kv_gather_prefix");

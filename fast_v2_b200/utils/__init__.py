@@ -2,7 +2,7 @@
 
 The reference's generation_functions.py imports these submodules by name
 (``from utils.static_kv_cache import StaticKVCache, StaticBlockCache`` ...);
-see ``fast_v2_b200.install_dropin`` or re-export stubs in the reference tree.
+see ``fast_v2_b200.dropin.install`` or re-export stubs in the reference tree.
 """
 from .attention_backends import (  # noqa: F401
     AttentionBackend,

@@ -116,7 +116,11 @@ int fdl_kv_scatter(void* k_dst, void* v_dst,
  * where row(b, t) = cu_seqlens[b] + t when cu_seqlens != NULL (packed varlen
  * output [sum_b(len[b]+n_blk), heads*rep, D]) and otherwise b*out_sb + t*out_ss
  * (padded output, e.g. the BHSD concat buffer).  len is device int32 [B]
- * bounded by prefix_cap; cu_seqlens is device int32 [B+1].
+ * bounded by prefix_cap; cu_seqlens is device int32 [B+1] and out_rows the
+ * number of rows of the packed output (ignored without cu_seqlens).  A
+ * sequence whose packed range [cu_seqlens[b], cu_seqlens[b+1]) is negative,
+ * reaches past out_rows or holds fewer than len[b] + n_blk rows is skipped
+ * whole and reported as FDL_DEV_INDEX (info = b).
  * Replaces the dynamic-path prefix concat torch.cat(prefix, block)
  * (modeling.py:390-392, :1410-1413, :1494-1495), the prefix views
  * StaticKVCache.get_kv_up_to / __getitem__ (utils/static_kv_cache.py:162-168,
@@ -127,6 +131,7 @@ int fdl_kv_gather_prefix(const void* k_prefix, const void* v_prefix,
                          const int32_t* len, int prefix_cap,
                          const void* k_block, const void* v_block, int n_blk,
                          void* k_out, void* v_out, const int32_t* cu_seqlens,
+                         int64_t out_rows,
                          int batch, int heads, int head_dim, int rep,
                          int elem_bytes,
                          int64_t pre_sb, int64_t pre_ss, int64_t pre_sh,

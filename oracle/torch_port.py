@@ -89,6 +89,14 @@ def rmsnorm(x, w, eps):
     return w * (h * torch.rsqrt(var + eps)).to(dt)
 
 
+def swiglu(gu):
+    """The activation of Fast_dLLM_QwenMLP.forward (modeling.py:163-165) on the
+    fused gate/up projection output [.., 2F]: act_fn(gate) * up with act_fn =
+    silu (Qwen2 hidden_act), in the tensor's dtype."""
+    f = gu.shape[-1] // 2
+    return F.silu(gu[..., :f]) * gu[..., f:]
+
+
 def rope(x_bhsd, cos, sin):
     """apply_rotary_pos_emb (modeling.py:186-199), BHSD with cos/sin [1, S, D]."""
     cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
