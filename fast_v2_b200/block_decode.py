@@ -134,6 +134,21 @@ class BlockDiffusionLM:
         _lib.count_launches(1)
         return q, k, v
 
+    def qkv_into(self, layer, x, pos, k_dst, v_dst, start=None, dst_pos=None, seq_dim: int = 1):
+        """As ``qkv``, but K and V go straight into their cache rows (the
+        reference's projection -> RoPE -> cache write, attention_backends.py:
+        937-955, as one kernel after the GEMM): k_dst / v_dst [B, S, Hkv, D]
+        (seq_dim 1) or [B, Hkv, S, D] (seq_dim 2), token t of sequence b at
+        dst_pos[b, t], else start[b] + t, else t.  Returns q."""
+        g = self.geo
+        B, T, _ = x.shape
+        y = torch.addmm(layer["bqkv"], x.view(B * T, -1), layer["wqkv"].t())
+        q = torch.empty(B, T, g.heads, g.head_dim, dtype=self.dtype, device=self.device)
+        torch.ops.fdl.rope_qkv_kv(y, pos.reshape(-1), self.inv_freq, g.heads, g.kv_heads, q, k_dst, v_dst, start,
+                                  dst_pos, seq_dim)
+        _lib.count_launches(1)
+        return q
+
     def add_rmsnorm(self, y, h, w):
         """Residual connection and the following RMSNorm in one kernel:
         h += y in place (bf16 rounding, the layer's `residual + hidden_states`)
@@ -181,9 +196,12 @@ class DecodeState:
     reallocated while decoding, so every step is CUDA-graph capturable."""
 
     def __init__(self, model: BlockDiffusionLM, batch: int, max_len: int, block: int = 32,
-                 sparse_keep: float | None = None):
+                 sparse_keep: float | None = None, fused_kv_store: bool = False):
         g, dev, dt = model.geo, model.device, model.dtype
         self.model, self.B, self.block, self.max_len = model, batch, block, max_len
+        # True: the RoPE kernel stores K/V into the cache / block buffer itself
+        # (fdl_rope_qkv_kv); False: RoPE, then a separate append / scatter.
+        self.fused_kv_store = fused_kv_store
         self.k = [torch.zeros(batch, max_len, g.kv_heads, g.head_dim, dtype=dt, device=dev) for _ in range(g.layers)]
         self.v = [torch.zeros_like(t) for t in self.k]
         self.blk_k = [torch.zeros(batch, g.kv_heads, block, g.head_dim, dtype=dt, device=dev) for _ in range(g.layers)]
@@ -207,19 +225,21 @@ class DecodeState:
         self.attn_ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev) if wsb > 0 else None
 
     # -------------------------------------------------------------- pieces
-    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos):
+    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos, lens=None):
         """Block attention for layer l: queries q [B, T, Hq, D] over the
-        committed prefix ("full") or the sparse prefix ("sparse") followed by
-        the given block K/V, under the block-causal mask."""
+        committed prefix ("full": the first `lens` rows of the cache, default
+        self.lens) or the sparse prefix ("sparse") followed by the given block
+        K/V (none when k_blk is None), under the block-causal mask."""
         g = self.model.geo
         out = torch.empty_like(q)
         if prefix == "sparse":
             kp, vp, lens = self.sp_k[l], self.sp_v[l], self.sp_len[l]
         else:
-            kp, vp, lens = self.k[l], self.v[l], self.lens
+            kp, vp, lens = self.k[l], self.v[l], self.lens if lens is None else lens
         T = q.shape[1]
+        n_blk = 0 if k_blk is None else k_blk.shape[1]
         ns = self.attn_splits if T <= self.block else _lib.attn_auto_splits(self.B, T, g.heads, g.kv_heads,
-                                                                            kp.shape[1], k_blk.shape[1])
+                                                                            kp.shape[1], n_blk)
         ws = self.attn_ws
         if ns > 1 and (ws is None or ws.numel() < _lib.attn_workspace_bytes(self.B, T, g.heads, ns)):
             ws = torch.empty(_lib.attn_workspace_bytes(self.B, T, g.heads, ns), dtype=torch.uint8, device=q.device)
@@ -249,7 +269,15 @@ class DecodeState:
         pos = pos.contiguous()
         qpos = pos.to(torch.int32).contiguous()
 
+        # Fused store: the span's K/V go into the cache at self.lens in the
+        # RoPE kernel; the attention then reads cache[:lens + T] under the
+        # block-causal mask (the same keys as prefix + span).
+        lens_after = self.lens + T if self.fused_kv_store else None
+
         def attend_layer(l, layer, x):
+            if self.fused_kv_store:
+                q = m.qkv_into(layer, x, pos, self.k[l], self.v[l], start=self.lens)
+                return self.attend(q, l, "full", None, None, qpos, lens=lens_after)
             q, k, v = m.qkv(layer, x, pos)
             a = self.attend(q, l, "full", k, v, qpos)
             torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
@@ -282,8 +310,13 @@ class DecodeState:
         qpos = p.to(torch.int32).contiguous()
 
         def attend_layer(l, layer, x):
-            q, k, v = m.qkv(layer, x, p)
             bk, bv = self.blk_k[l], self.blk_v[l]
+            if self.fused_kv_store:
+                # K/V of the computed positions go straight into the block
+                # buffer (BHSD): 0..blk-1 on a full step, fed[b, i] on a cached one.
+                q = m.qkv_into(layer, x, p, bk, bv, dst_pos=fed, seq_dim=2)
+                return self.attend(q, l, prefix, bk.transpose(1, 2), bv.transpose(1, 2), qpos)
+            q, k, v = m.qkv(layer, x, p)
             if fed is None:
                 torch.ops.fdl.kv_append([bk.transpose(1, 2)], [bv.transpose(1, 2)], [k], [v], self.zero)
             else:
@@ -330,7 +363,7 @@ class BlockDiffusionDecoder:
     def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
                  sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
                  fed_bucket: int = 1, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
-                 use_graphs: bool = False):
+                 use_graphs: bool = False, fused_kv_store: bool = False):
         assert prompt_len % block == 0 and block % sub_block == 0
         self.m, self.B, self.block, self.sub = model, batch, block, sub_block
         self.threshold, self.refresh, self.fed_bucket = threshold, refresh, fed_bucket
@@ -338,7 +371,7 @@ class BlockDiffusionDecoder:
         self.prompt_len, self.gen_len = prompt_len, gen_len
         max_len = prompt_len + gen_len + block
         max_len = (max_len + 255) // 256 * 256
-        self.st = DecodeState(model, batch, max_len, block, sparse_keep)
+        self.st = DecodeState(model, batch, max_len, block, sparse_keep, fused_kv_store)
         self.prefix = "sparse" if sparse_keep else "full"
         dev = model.device
         self.ar = torch.arange(block, device=dev)
@@ -440,6 +473,8 @@ class BlockDiffusionDecoder:
         with torch.cuda.stream(s):
             fn()
         torch.cuda.current_stream().wait_stream(s)
+        # A warm-up whose kernels recorded an error is not captured.
+        _lib.check_device(f"BlockDiffusionDecoder capture warm-up of step {key!r}")
         for t, v in zip(bufs, snap):
             t.copy_(v)
         g = torch.cuda.CUDAGraph()

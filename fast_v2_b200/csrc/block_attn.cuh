@@ -65,6 +65,27 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 #define FDL_ATTN_PREFETCH 1
 #endif
 constexpr int kPrefetch = FDL_ATTN_PREFETCH;  // key tiles prefetched into L2 ahead of the smem ring
+#ifndef FDL_ATTN_POLY
+#define FDL_ATTN_POLY 0
+#endif
+// Of every 8 exponential pairs of a full key tile, kPolyPairs are computed on
+// the FMA pipe (ptx::exp2_poly2) and the rest on the special-function unit.
+constexpr int kPolyPairs = FDL_ATTN_POLY;
+static_assert(kPolyPairs >= 0 && kPolyPairs <= 8, "polynomial share in eighths");
+// Pair i of a 16-pair chunk goes to the FMA pipe when (i * kPolyPairs) % 8 <
+// kPolyPairs: the chosen pairs are spread evenly through the chunk.
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return (i * kPolyPairs) % 8 < kPolyPairs; }
+// 2^x of a packed pair, by the polynomial or by two special-function ex2.
+template <bool POLY>
+__device__ __forceinline__ uint64_t exp2_pair(uint64_t x2) {
+  if constexpr (POLY) {
+    return ptx::exp2_poly2(x2);
+  } else {
+    float x0, x1;
+    ptx::unpack2(x2, x0, x1);
+    return ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
+  }
+}
 
 constexpr uint32_t kSmemQ = 0;                        // 2 halves x 256 rows x 128 B
 constexpr uint32_t kQHalf = 256 * 128;                // 32 KB
@@ -509,9 +530,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-              float x0, x1;
-              ptx::unpack2(x2, x0, x1);
-              const uint64_t e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
+              const uint64_t e2 = poly_pair(i) ? exp2_pair<true>(x2) : exp2_pair<false>(x2);
               acc2 = ptx::add2(acc2, e2);
               float p0, p1;
               ptx::unpack2(e2, p0, p1);
@@ -637,9 +656,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-            float x0, x1;
-            ptx::unpack2(x2, x0, x1);
-            const uint64_t e2 = ptx::pack2(ptx::ex2(x0), ptx::ex2(x1));
+            const uint64_t e2 = poly_pair(i) ? exp2_pair<true>(x2) : exp2_pair<false>(x2);
             acc2 = ptx::add2(acc2, e2);
             float p0, p1;
             ptx::unpack2(e2, p0, p1);
