@@ -37,6 +37,7 @@ EXPORTS = (
     "fdl_cosine_select",
     "fdl_focus_select",
     "fdl_focus_importance",
+    "fdl_softmax_argmax",
     "fdl_last_device_error",
     "fdl_version",
 )

@@ -388,6 +388,8 @@ class BlockDiffusionDecoder:
         self.nxt = torch.zeros(B, 1, dtype=torch.long, device=dev)
         self.status_h = torch.zeros(2, dtype=torch.long).pin_memory() if dev.type == "cuda" else torch.zeros(2, dtype=torch.long)
         self.src_idx = torch.zeros(sub_block, dtype=torch.long, device=dev)
+        self.x1_buf = torch.zeros(B, sub_block, dtype=torch.long, device=dev)
+        self.p_buf = torch.zeros(B, sub_block, dtype=model.dtype, device=dev)
         self._subs = [torch.arange(s, s + sub_block, device=dev) for s in range(0, block, sub_block)]
         self._srcs = [torch.clamp(t - 1, min=0) for t in self._subs]
         self.use_graphs = use_graphs
@@ -402,10 +404,15 @@ class BlockDiffusionDecoder:
         Logits only for the rows the sampler reads: row i of the sub-block is
         predicted by position i-1 (row 0 by itself).  As sample_with_top_p at
         temperature 0 (modeling.py:2263-2269): softmax in the logits dtype,
-        argmax = first maximal probability."""
+        argmax = first maximal probability (fdl_softmax_argmax)."""
         m = self.m
         hn = m.rmsnorm(h.index_select(1, self.src_idx).contiguous(), m.norm)
-        p, x1 = torch.softmax(m.logits_rows(hn), dim=-1).max(-1)
+        # One fused pass over each logits row gives the argmax of the bf16
+        # softmax (ties to the lower index) and its probability, without the
+        # [B, sub, vocab] probabilities.
+        p, x1 = self.p_buf, self.x1_buf
+        torch.ops.fdl.softmax_argmax(m.logits_rows(hn), x1, p)
+        _lib.count_launches(1)
         sub = self.x.index_select(1, self.sub_idx)
         mask_idx = sub == self.mask_id
         x1p = torch.where(mask_idx, p, torch.full_like(p, -math.inf))

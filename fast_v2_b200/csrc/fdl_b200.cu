@@ -13,6 +13,7 @@
 #include "block_attn.cuh"
 #include "rope_swiglu.cuh"
 #include "token_select.cuh"
+#include "sampling.cuh"
 
 using namespace fdl;
 
@@ -643,6 +644,18 @@ int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int64_t
   SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn};
   const dim3 grid(static_cast<unsigned>(rows), (ffn / 8 + kSwigluChunk - 1) / kSwigluChunk);
   swiglu_kernel<<<grid, kSwigluThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+int fdl_softmax_argmax(const void* logits, int64_t row_stride, int rows, int vocab, int64_t* token, void* prob,
+                       fdl_stream_t stream) {
+  if (rows < 0 || rows > INT32_MAX || vocab < 1 || row_stride < vocab) return FDL_E_SHAPE;
+  if (rows == 0) return FDL_OK;
+  if (!logits || !token) return FDL_E_NULL;
+  if (!aligned16(logits) || (row_stride * 2) % 16) return FDL_E_ALIGN;
+  SampleArgs a{static_cast<const __nv_bfloat16*>(logits), row_stride, vocab, token,
+               static_cast<__nv_bfloat16*>(prob)};
+  softmax_argmax_kernel<<<static_cast<unsigned>(rows), kSampleThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }
 

@@ -566,6 +566,29 @@ void swiglu(const Tensor& gu, const Tensor& out) {
            "swiglu");
 }
 
+// logits [..., V] bf16 with uniformly strided rows; token int64 and prob bf16
+// hold one entry per row (any shape with that many contiguous elements).
+void softmax_argmax(const Tensor& logits, const Tensor& token, const std::optional<Tensor>& prob) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.stride(-1) == 1,
+              "fdl.softmax_argmax: logits must be a bf16 CUDA tensor with unit inner stride");
+  const int64_t V = logits.size(-1);
+  const int64_t rows = V > 0 ? logits.numel() / V : 0;
+  for (int64_t d = 0; d + 2 < logits.dim(); ++d)
+    TORCH_CHECK(logits.stride(d) == logits.size(d + 1) * logits.stride(d + 1),
+                "fdl.softmax_argmax: logits rows must be uniformly strided");
+  TORCH_CHECK(token.is_cuda() && token.scalar_type() == at::kLong && token.is_contiguous() && token.numel() == rows,
+              "fdl.softmax_argmax: token must be a contiguous CUDA int64 tensor with one entry per row");
+  if (prob)
+    TORCH_CHECK(prob->is_cuda() && prob->scalar_type() == at::kBFloat16 && prob->is_contiguous() &&
+                    prob->numel() == rows,
+                "fdl.softmax_argmax: prob must be a contiguous CUDA bf16 tensor with one entry per row");
+  c10::cuda::CUDAGuard guard(logits.device());
+  check_rc(fdl_softmax_argmax(logits.data_ptr(), logits.dim() >= 2 ? logits.stride(-2) : V, static_cast<int>(rows),
+                              static_cast<int>(V), token.data_ptr<int64_t>(), prob ? prob->data_ptr() : nullptr,
+                              cur_stream()),
+           "softmax_argmax");
+}
+
 // x, res, sum_out, normed: [..., H] with uniformly strided rows.  sum_out
 // may be res itself (in-place residual update) or absent.
 void add_rmsnorm(const Tensor& x, const Tensor& res, const std::optional<Tensor>& weight, double eps,
@@ -649,6 +672,7 @@ TORCH_LIBRARY(fdl, m) {
   m.def("rope_qkv_kv(Tensor y, Tensor pos, Tensor inv_freq, int hq, int hkv, Tensor(a!) q, Tensor(b!) k_dst, "
         "Tensor(c!) v_dst, Tensor? start, Tensor? dst_pos, int seq_dim) -> ()");
   m.def("swiglu(Tensor gu, Tensor(a!) out) -> ()");
+  m.def("softmax_argmax(Tensor logits, Tensor(a!) token, Tensor(b!)? prob) -> ()");
   m.def("add_rmsnorm(Tensor x, Tensor res, Tensor? weight, float eps, Tensor(a!)? sum_out, Tensor(b!) normed) -> ()");
 }
 
@@ -668,6 +692,7 @@ TORCH_LIBRARY_IMPL(fdl, CUDA, m) {
   m.impl("rope_qkv", &rope_qkv);
   m.impl("rope_qkv_kv", &rope_qkv_kv);
   m.impl("swiglu", &swiglu);
+  m.impl("softmax_argmax", &softmax_argmax);
   m.impl("add_rmsnorm", &add_rmsnorm);
 }
 
@@ -699,6 +724,7 @@ TORCH_LIBRARY_IMPL(fdl, Meta, m) {
   m.impl("rope_qkv_kv", [](const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, const Tensor&, const Tensor&,
                            const Tensor&, const std::optional<Tensor>&, const std::optional<Tensor>&, int64_t) {});
   m.impl("swiglu", [](const Tensor&, const Tensor&) {});
+  m.impl("softmax_argmax", [](const Tensor&, const Tensor&, const std::optional<Tensor>&) {});
   m.impl("add_rmsnorm", [](const Tensor&, const Tensor&, const std::optional<Tensor>&, double,
                            const std::optional<Tensor>&, const Tensor&) {});
 }

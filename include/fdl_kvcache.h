@@ -421,6 +421,24 @@ int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs,
                int64_t rows, int ffn, fdl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Greedy sampling statistics over the vocabulary (bf16 logits).
+ *
+ * For every row r < rows of logits [rows, vocab] (row stride in elements):
+ *   m = max_v l_v,  s = sum_v exp(l_v - m)   (fp32),
+ *   prob[r]  = bf16(exp(0) / s)               (the largest probability),
+ *   token[r] = the first v with bf16(exp(l_v - m) / s) == prob[r].
+ * That is the argmax of the bf16 softmax with ties to the lower index, and
+ * the probability gathered at it: sample_with_top_p at temperature 0
+ * (modeling.py:2263-2269) and the x1_p gather of the samplers
+ * (generation_functions.py:2290-2291), without the [rows, vocab]
+ * probabilities.  prob may be NULL.  A row with no finite logit gets token 0
+ * and is reported as FDL_DEV_INDEX (info = row).
+ * ---------------------------------------------------------------------- */
+int fdl_softmax_argmax(const void* logits, int64_t row_stride, int rows,
+                       int vocab, int64_t* token, void* prob,
+                       fdl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Status.  Copies the calling device's first recorded device-side error
  * code into *code and the offending value into *info (either may be NULL),
  * then clears both.  Synchronises the device.  Returns 0 or -(cudaError_t).

@@ -390,3 +390,26 @@ def ceil_div(a: int, b: int) -> int:
 
 
 __all__ = [n for n in dir() if not n.startswith("_") and n not in ("annotations", "math", "np")]
+
+
+# --------------------------------------------------------------------------
+# greedy sampling statistics
+# --------------------------------------------------------------------------
+
+
+def softmax_argmax_bf16(logit_bits):
+    """sample_with_top_p at temperature 0 (modeling.py:2263-2269) and the
+    gathered probability of its token (generation_functions.py:2290-2291) on
+    bf16 logits [rows, V] (uint16 bit patterns): probabilities
+    bf16(exp(l - m) / s) with m the row max and s = sum exp(l - m) (float64
+    here), token = the first index of the largest probability (argmax's
+    first-occurrence rule), prob = that probability.  Returns (token int64
+    [rows], prob bf16 bits [rows])."""
+    x = bf16_to_f32(np.ascontiguousarray(logit_bits)).astype(np.float64)
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp(x - m)
+    s = e.sum(axis=-1, keepdims=True)
+    p = f32_to_bf16((e / s).astype(np.float32))
+    pf = bf16_to_f32(p)
+    tok = pf.argmax(axis=-1).astype(np.int64)
+    return tok, np.take_along_axis(p, tok[:, None], axis=-1)[:, 0]

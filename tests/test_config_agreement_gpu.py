@@ -43,13 +43,14 @@ def _ref_layers(model):
     return out
 
 
+@pytest.mark.parametrize("fused", [False, True], ids=["separate_store", "fused_store"])
 @pytest.mark.parametrize("name,geo,batch,prompt_len", [("config4_1.5b", QWEN25_1_5B, 4, 96),
                                                         ("config5_7b", QWEN25_7B, 4, 64)])
-def test_full_dkv_step_greedy_agreement_at_benchmark_geometry(name, geo, batch, prompt_len):
+def test_full_dkv_step_greedy_agreement_at_benchmark_geometry(name, geo, batch, prompt_len, fused):
     torch.manual_seed(0)
     model = BlockDiffusionLM(geo, device=DEV, seed=123)
     model.lm_head[MASK_ID].zero_()
-    dec = BlockDiffusionDecoder(model, batch, prompt_len, 64)
+    dec = BlockDiffusionDecoder(model, batch, prompt_len, 64, fused_kv_store=fused)
     g = torch.Generator().manual_seed(5)
     prompt = torch.randint(0, 151643, (batch, prompt_len), generator=g).to(DEV)
     geod = dict(head_dim=geo.head_dim, heads=geo.heads, kv_heads=geo.kv_heads, rope_theta=geo.rope_theta,

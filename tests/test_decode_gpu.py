@@ -28,6 +28,11 @@ DEV = torch.device("cuda")
 NEAR_TIE_ULPS = 2.0
 
 
+# Both ways of writing a forward's K/V: stored by the RoPE kernel itself
+# (fdl_rope_qkv_kv), or a separate append / scatter after it.
+KV_STORE = pytest.mark.parametrize("fused", [False, True], ids=["separate_store", "fused_store"])
+
+
 def _bf16_ulp(x: np.ndarray) -> np.ndarray:
     a = np.maximum(np.abs(x), 1e-30)
     return np.exp2(np.floor(np.log2(a)) - 7)
@@ -46,8 +51,9 @@ def _setup(gen=None, **kw):
     return g, model, dec, prompt
 
 
-def test_teacher_forced_logits_argmax_match_reference():
-    g, m, dec, prompt = _setup()
+@KV_STORE
+def test_teacher_forced_logits_argmax_match_reference(fused):
+    g, m, dec, prompt = _setup(fused_kv_store=fused)
     st = dec.st
     st.lens.zero_()
     seed = None
@@ -89,8 +95,9 @@ def test_teacher_forced_logits_argmax_match_reference():
     assert frac >= floor - 0.005, f"argmax mismatches outside near ties (trace, kind, b, pos, gap): {worst[:10]}"
 
 
-def test_free_running_greedy_agreement_reported():
-    g, m, dec, prompt = _setup()
+@KV_STORE
+def test_free_running_greedy_agreement_reported(fused):
+    g, m, dec, prompt = _setup(fused_kv_store=fused)
     with torch.no_grad():
         out, finished = dec.generate(prompt)
     ref = g["tokens_bf16"]
@@ -108,11 +115,12 @@ def test_free_running_greedy_agreement_reported():
     assert _lib.last_device_error()[0] == 0
 
 
-def test_graph_replay_decode_identical_to_eager():
-    g, m, dec, prompt = _setup(gen=64)
+@KV_STORE
+def test_graph_replay_decode_identical_to_eager(fused):
+    g, m, dec, prompt = _setup(gen=64, fused_kv_store=fused)
     with torch.no_grad():
         eager, _ = dec.generate(prompt, n_blocks=2)
-        _, _, dec_g, _ = _setup(gen=64, use_graphs=True)
+        _, _, dec_g, _ = _setup(gen=64, use_graphs=True, fused_kv_store=fused)
         dec_g.m = m
         dec_g.st.model = m
         dec_g.capture_all()
@@ -120,8 +128,9 @@ def test_graph_replay_decode_identical_to_eager():
     assert torch.equal(eager, graphed)
 
 
-def test_sparse_prefix_decode_runs_and_keeps_quarter():
-    g, m, dec, prompt = _setup(gen=64, sparse_keep=0.25)
+@KV_STORE
+def test_sparse_prefix_decode_runs_and_keeps_quarter(fused):
+    g, m, dec, prompt = _setup(gen=64, sparse_keep=0.25, fused_kv_store=fused)
     with torch.no_grad():
         out, _ = dec.generate(prompt, n_blocks=2)
     P = prompt.shape[1]
@@ -130,3 +139,23 @@ def test_sparse_prefix_decode_runs_and_keeps_quarter():
     # the sparse prefix selected for the second block held ceil(0.25 * (P + 32)) tokens
     assert int(dec.st.sp_len[0][0]) == -(-(P + 32) // 4)
     assert _lib.last_device_error()[0] == 0
+
+
+def test_fused_store_writes_the_same_cache_as_separate_store():
+    """After the prompt prefill, layer 0's committed K/V rows (which depend on
+    the embeddings alone) are the same whichever way they were written -- by
+    the RoPE kernel's own store or by RoPE then append: the store is a copy,
+    bit for bit.  Deeper layers see attention outputs whose split-KV choice
+    differs between the two paths, so only their shape and finiteness are
+    compared."""
+    out = {}
+    for fused in (False, True):
+        g, m, dec, prompt = _setup(gen=64, fused_kv_store=fused)
+        with torch.no_grad():
+            dec.prefill(prompt)
+        n = int(dec.st.lens[0])
+        assert n == prompt.shape[1]
+        out[fused] = (dec.st.k[0][:, :n].clone(), dec.st.v[0][:, :n].clone(),
+                      [torch.isfinite(t[:, :n].float()).all().item() for t in dec.st.k + dec.st.v])
+    assert torch.equal(out[False][0], out[True][0]) and torch.equal(out[False][1], out[True][1])
+    assert all(out[True][2]) and all(out[False][2])
