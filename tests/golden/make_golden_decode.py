@@ -120,6 +120,12 @@ def build_reference_model(modeling, cfg_cls, dtype):
                   max_position_embeddings=4096, rope_theta=geo.rope_theta, rms_norm_eps=geo.eps,
                   tie_word_embeddings=False, bd_size=32, attn_implementation="sdpa")
     model = modeling.Fast_dLLM_QwenForCausalLM(cfg).to(dtype).eval()
+    # The rotary inverse frequencies stay fp32, as from_pretrained(torch_dtype=
+    # bfloat16) leaves them (computed in fp32 at init, not in the checkpoint);
+    # model.to(dtype) above would have rounded the buffer to bf16.
+    rot = model.model.rotary_emb
+    rot.inv_freq = 1.0 / (geo.rope_theta ** (torch.arange(0, geo.head_dim, 2, dtype=torch.int64).float()
+                                             / geo.head_dim))
     q_out, kv_out = geo.heads * geo.head_dim, geo.kv_heads * geo.head_dim
     with torch.no_grad():
         model.model.embed_tokens.weight.copy_(ours.embed)
