@@ -431,12 +431,12 @@ def _e2e(args, rank, world, kt, geo_name):
                 "threshold": 0.9, "cache": cache_desc, "step": "one 32-token block (diffusion steps + commit)",
                 "weights": "random normal(0, 0.02); lm_head row of the mask token zeroed",
                 "fed_bucket": getattr(args, "fed_bucket", 1),
-                "kv_store": ("fused into the RoPE kernel" if getattr(args, "kv_store", "separate") == "fused"
+                "kv_store": ("fused into the RoPE kernel" if getattr(args, "kv_store", "fused") == "fused"
                              else "separate append/scatter"),
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
                                                       fed_bucket=getattr(args, "fed_bucket", 1), use_graphs=True,
-                                                      fused_kv_store=getattr(args, "kv_store", "separate") == "fused")
+                                                      fused_kv_store=getattr(args, "kv_store", "fused") == "fused")
     if not cpu_only:
         # One seeded global batch of B x world prompts; each rank decodes its
         # own contiguous shard of sequences (sequence_shard), as the
@@ -944,7 +944,7 @@ def main():
     ap.add_argument("--norm-only", action="store_true", help="gather_norm: write only the normed rows")
     ap.add_argument("--fed-bucket", type=int, default=1,
                     help="cached dKV steps run at the fed width rounded up to this multiple (1 = exact, as the reference)")
-    ap.add_argument("--kv-store", choices=["fused", "separate"], default="separate",
+    ap.add_argument("--kv-store", choices=["fused", "separate"], default="fused",
                     help="e2e: 'fused' = the RoPE kernel stores K/V into the cache itself; 'separate' = RoPE, then "
                          "an append / scatter launch")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -196,7 +196,7 @@ class DecodeState:
     reallocated while decoding, so every step is CUDA-graph capturable."""
 
     def __init__(self, model: BlockDiffusionLM, batch: int, max_len: int, block: int = 32,
-                 sparse_keep: float | None = None, fused_kv_store: bool = False):
+                 sparse_keep: float | None = None, fused_kv_store: bool = True):
         g, dev, dt = model.geo, model.device, model.dtype
         self.model, self.B, self.block, self.max_len = model, batch, block, max_len
         # True: the RoPE kernel stores K/V into the cache / block buffer itself
@@ -363,7 +363,7 @@ class BlockDiffusionDecoder:
     def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
                  sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
                  fed_bucket: int = 1, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
-                 use_graphs: bool = False, fused_kv_store: bool = False):
+                 use_graphs: bool = False, fused_kv_store: bool = True):
         assert prompt_len % block == 0 and block % sub_block == 0
         self.m, self.B, self.block, self.sub = model, batch, block, sub_block
         self.threshold, self.refresh, self.fed_bucket = threshold, refresh, fed_bucket

@@ -641,8 +641,12 @@ int fdl_swiglu(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int64_t
   if (rows == 0) return FDL_OK;
   if (!gu || !out) return FDL_E_NULL;
   if (!aligned16(gu) || !aligned16(out) || (gu_rs * 2) % 16 || (out_rs * 2) % 16) return FDL_E_ALIGN;
-  SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn};
-  const dim3 grid(static_cast<unsigned>(rows), (ffn / 8 + kSwigluChunk - 1) / kSwigluChunk);
+  const uint64_t total = static_cast<uint64_t>(rows) * (ffn / 8);
+  if (total >= (1ull << 31)) return FDL_E_SHAPE;
+  SwigluArgs a{static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, rows, ffn,
+               static_cast<uint32_t>(total), {}};
+  a.vpr.init(static_cast<uint32_t>(ffn / 8));
+  const unsigned grid = static_cast<unsigned>((total + kSwigluChunk - 1) / kSwigluChunk);
   swiglu_kernel<<<grid, kSwigluThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }

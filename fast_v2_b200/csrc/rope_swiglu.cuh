@@ -176,6 +176,8 @@ struct SwigluArgs {
   int64_t out_rs;
   int64_t rows;
   int F;
+  uint32_t total;           // rows * F / 8 vectors
+  FastDiv vpr;              // F / 8 vectors per row
 };
 
 // bf16(silu(x)) exactly as torch computes it for a bf16 tensor: fp32
@@ -206,31 +208,33 @@ __device__ __forceinline__ float silu_bf16(float x) {
   return bf16r(s);
 }
 
-// Grid (rows, chunks): a CTA covers kSwigluUnroll * 256 vectors of 8
-// elements of one row; every thread issues all of its loads before any
-// arithmetic so each SM keeps enough bytes in flight to stream from HBM.
+// The rows x (F / 8) vectors of the output form one flat range; CTA c
+// covers vectors [c * kSwigluChunk, (c + 1) * kSwigluChunk) across row
+// boundaries, so every CTA but the last is full (a per-row grid leaves the
+// last chunk of every row part-empty: 320 of 1024 vectors at F = 18944).
+// Every thread issues all of its loads before any arithmetic so each SM keeps
+// enough bytes in flight to stream from HBM.
 constexpr int kSwigluUnroll = 4;
 constexpr int kSwigluChunk = kSwigluUnroll * kSwigluThreads;  // vectors per CTA
 
 __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const __grid_constant__ SwigluArgs a) {
-  const int vpr = a.F / 8;
-  const int64_t r = blockIdx.x;
-  const int v0 = blockIdx.y * kSwigluChunk + threadIdx.x;
-  const __nv_bfloat16* row = a.gu + r * a.gu_rs;
-  __nv_bfloat16* orow = a.out + r * a.out_rs;
+  const uint32_t i0 = blockIdx.x * kSwigluChunk + threadIdx.x;
   uint4 ug[kSwigluUnroll], uu[kSwigluUnroll];
+  uint32_t rr[kSwigluUnroll], vv[kSwigluUnroll];
 #pragma unroll
   for (int k = 0; k < kSwigluUnroll; ++k) {
-    const int v = v0 + k * kSwigluThreads;
-    if (v < vpr) {
-      ug[k] = ld_stream16(reinterpret_cast<const char*>(row + v * 8));
-      uu[k] = ld_stream16(reinterpret_cast<const char*>(row + a.F + v * 8));
+    const uint32_t i = i0 + k * kSwigluThreads;
+    if (i < a.total) {
+      a.vpr.divmod(i, rr[k], vv[k]);
+      const __nv_bfloat16* row = a.gu + static_cast<int64_t>(rr[k]) * a.gu_rs;
+      ug[k] = ld_stream16(reinterpret_cast<const char*>(row + vv[k] * 8));
+      uu[k] = ld_stream16(reinterpret_cast<const char*>(row + a.F + vv[k] * 8));
     }
   }
 #pragma unroll
   for (int k = 0; k < kSwigluUnroll; ++k) {
-    const int v = v0 + k * kSwigluThreads;
-    if (v < vpr) {
+    const uint32_t i = i0 + k * kSwigluThreads;
+    if (i < a.total) {
       const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(&ug[k]);
       const __nv_bfloat16* u = reinterpret_cast<const __nv_bfloat16*>(&uu[k]);
       uint4 o;
@@ -238,7 +242,7 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const __grid_con
 #pragma unroll
       for (int e = 0; e < 8; ++e)
         y[e] = __float2bfloat16_rn(__fmul_rn(silu_bf16(__bfloat162float(g[e])), __bfloat162float(u[e])));
-      *reinterpret_cast<uint4*>(orow + v * 8) = o;
+      *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(rr[k]) * a.out_rs + vv[k] * 8) = o;
     }
   }
 }
