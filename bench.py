@@ -469,6 +469,26 @@ def _e2e(args, rank, world, kt, geo_name):
                 state["gen"] = []
                 torch.cuda.synchronize()
 
+        def full_generation():
+            """The reference's own tokens/s definition (eval.py:425-429,
+            515-519): one whole generation -- the prompt prefill plus every
+            block of the configured generation length -- from a fresh cache.
+            Returns (generated tokens, device ms)."""
+            n_blk = G // 32  # the cache holds prompt + G + one block
+            torch.cuda.synchronize()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            with torch.no_grad():
+                bridge = dec.prefill(prompt)
+                gen_blocks = []
+                for _ in range(n_blk):
+                    blk, bridge = dec.decode_block(bridge, stats=stats)
+                    gen_blocks.append(blk)
+            e0.record()
+            torch.cuda.synchronize()
+            state["bridge"], state["blocks"], state["gen"] = bridge, n_blk, gen_blocks
+            return B * 32 * n_blk, s0.elapsed_time(e0)
+
         def collect():
             """This rank's generated sequences since the last prefill: prompt
             followed by every decoded 32-token block."""
@@ -545,7 +565,7 @@ def _e2e(args, rank, world, kt, geo_name):
         return dict(meta, cpu_sample=cpu_sample)
     kvb, fl = dom_work()
     return dict(meta, units_per_step=B * 32, step=step, dominant=dominant, graph=False, e2e_step=e2e_step,
-                collect=collect, reserve=reserve,
+                collect=collect, reserve=reserve, full_generation=full_generation,
                 e2e_bytes=(B * 8, B * 32 * 8),
                 roofline=dict(bound="hbm", per_launch=kvb, kernel="block_attn_kernel (full dKV step, layer 0)",
                               flops=fl, dynamic=dom_work),
@@ -1004,6 +1024,16 @@ def main():
                "h2d_bytes_per_step": w["e2e_bytes"][0], "d2h_bytes_per_step": w["e2e_bytes"][1]}
         _fdl_lib.check_device("bench end-to-end region")
 
+    # One whole generation (prefill + all blocks), as the reference counts
+    # tokens/s; device time, max over ranks.
+    full_gen = None
+    if w.get("full_generation") is not None:
+        toks, fms = w["full_generation"]()
+        fms = max_over_ranks(fms, world)
+        full_gen = {"value": toks * world / (fms / 1e3), "unit": "tokens/s", "generated_tokens": toks * world,
+                    "seconds": fms / 1e3, "includes": "prompt prefill + every 32-token block of the generation"}
+        _fdl_lib.check_device("bench full generation")
+
     # Roofline of the dominant kernel.  Kernel-level configs: the config's own
     # kernel.  e2e configs: the largest kernel of this library in the step by
     # device time (attribution from one untimed, traced block), timed alone at
@@ -1097,6 +1127,8 @@ def main():
                              if meta["launches_per_step"] is not None else launches_timed),
             "device_status": 0,
         }
+        if full_gen is not None:
+            line["full_generation"] = full_gen
         if kernels is not None:
             line["kernels"] = kernels
         print(json.dumps(line), flush=True)

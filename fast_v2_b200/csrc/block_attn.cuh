@@ -66,10 +66,13 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 #endif
 constexpr int kPrefetch = FDL_ATTN_PREFETCH;  // key tiles prefetched into L2 ahead of the smem ring
 #ifndef FDL_ATTN_POLY
-#define FDL_ATTN_POLY 0
+#define FDL_ATTN_POLY 2
 #endif
-// Of every 8 exponential pairs of a full key tile, kPolyPairs are computed on
-// the FMA pipe (ptx::exp2_poly2) and the rest on the special-function unit.
+// Of every 8 exponential pairs of a full key tile of the one-row-tile
+// pipeline, kPolyPairs are computed on the FMA pipe (ptx::exp2_poly2) and the
+// rest on the special-function unit (measured on B200: +3% on 8-row
+// sub-blocks at 2 of 8; the two-row-tile pipeline is 3-9% slower with any
+// share, so it keeps every exponential on the special-function unit).
 constexpr int kPolyPairs = FDL_ATTN_POLY;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 8, "polynomial share in eighths");
 // Pair i of a 16-pair chunk goes to the FMA pipe when (i * kPolyPairs) % 8 <
@@ -656,7 +659,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint64_t x2 = ptx::fma2(ptx::pack2(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
-            const uint64_t e2 = poly_pair(i) ? exp2_pair<true>(x2) : exp2_pair<false>(x2);
+            const uint64_t e2 = exp2_pair<false>(x2);
             acc2 = ptx::add2(acc2, e2);
             float p0, p1;
             ptx::unpack2(e2, p0, p1);

@@ -11,8 +11,7 @@
 
 namespace fdl {
 
-constexpr int kNormThreads = 128;       // generic path: 4 rows per CTA
-constexpr int kNormMaxWarps = 16;       // vector path: up to 16 rows (warps) per CTA
+constexpr int kNormThreads = 128;  // 4 rows per CTA
 
 struct NormArgs {
   const char* x;
@@ -58,20 +57,15 @@ __device__ __forceinline__ T norm_elem(float x, float inv, const T* w, int i) {
   }
 }
 
-// Rows longer than 16 vectors per lane keep 4-warp CTAs (their registers do
-// not fit 16 warps).
-template <int VPL>
-constexpr int norm_max_warps() { return VPL > 16 ? 4 : kNormMaxWarps; }
-
 template <typename T, int VPL>
-__global__ void __launch_bounds__(norm_max_warps<VPL>() * 32) gather_rmsnorm_kernel(const __grid_constant__ NormArgs a) {
+__global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_kernel(const __grid_constant__ NormArgs a) {
   constexpr int EPV = 16 / sizeof(T);  // elements per 16-byte vector
-  // The weight row is staged once per CTA in shared memory (the rows of the
-  // CTA share it), so the output phase reads it at shared-memory latency
+  // The weight row is staged once per CTA in shared memory (the four rows of
+  // the CTA share it), so the output phase reads it at shared-memory latency
   // without holding it in registers through the reduction.
   __shared__ uint4 w_s[32 * VPL];
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
   const int nvec = a.H / EPV;
   bool live = row < a.B * a.T;
   int b = 0, t = 0;
@@ -98,7 +92,7 @@ __global__ void __launch_bounds__(norm_max_warps<VPL>() * 32) gather_rmsnorm_ker
   // loads, so its L2 latency overlaps them instead of preceding the index
   // load.
   if (a.w)
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) w_s[i] = *reinterpret_cast<const uint4*>(a.w + i * 16);
+    for (int i = threadIdx.x; i < nvec; i += kNormThreads) w_s[i] = *reinterpret_cast<const uint4*>(a.w + i * 16);
   float acc = 0.f;
   if (live) {
     if (a.res) {
@@ -265,35 +259,23 @@ __global__ void __launch_bounds__(kNormThreads) gather_rmsnorm_generic_kernel(co
   }
 }
 
-// Rows (warps) per CTA of the vector path.  A launch whose rows fit in one
-// wave at up to kNormMaxWarps rows per SM gets one CTA per SM with the rows
-// spread evenly (2048 rows on 148 SMs: 14 per SM, instead of 3 or 4 CTAs of 4
-// rows, where the SMs holding 16 rows set the time); larger launches use
-// full CTAs.
-inline int norm_warps_per_cta(int rows, int max_warps) {
-  const int sms = num_sms();
-  const int per_sm = (rows + sms - 1) / sms;
-  return per_sm < 1 ? 1 : (per_sm > max_warps ? max_warps : per_sm);
-}
-
 template <typename T>
 inline void launch_gather_rmsnorm(const NormArgs& a, bool vec_ok, cudaStream_t s) {
   const int rows = a.B * a.T;
+  const dim3 grid((rows + 3) / 4);
   const int nvec = a.H * static_cast<int>(sizeof(T)) / 16;
   if (!vec_ok || nvec > 32 * 32) {
-    gather_rmsnorm_generic_kernel<T><<<(rows + 3) / 4, kNormThreads, 0, s>>>(a);
+    gather_rmsnorm_generic_kernel<T><<<grid, kNormThreads, 0, s>>>(a);
     return;
   }
   const int vpl = (nvec + 31) / 32;
-  const int wpc = norm_warps_per_cta(rows, vpl > 16 ? 4 : kNormMaxWarps);
-  const dim3 grid((rows + wpc - 1) / wpc), block(32 * wpc);
-  if (vpl <= 2) gather_rmsnorm_kernel<T, 2><<<grid, block, 0, s>>>(a);
-  else if (vpl <= 4) gather_rmsnorm_kernel<T, 4><<<grid, block, 0, s>>>(a);
-  else if (vpl <= 8) gather_rmsnorm_kernel<T, 8><<<grid, block, 0, s>>>(a);
-  else if (vpl <= 14) gather_rmsnorm_kernel<T, 14><<<grid, block, 0, s>>>(a);
-  else if (vpl <= 16) gather_rmsnorm_kernel<T, 16><<<grid, block, 0, s>>>(a);
-  else if (vpl <= 28) gather_rmsnorm_kernel<T, 28><<<grid, block, 0, s>>>(a);
-  else gather_rmsnorm_kernel<T, 32><<<grid, block, 0, s>>>(a);
+  if (vpl <= 2) gather_rmsnorm_kernel<T, 2><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 4) gather_rmsnorm_kernel<T, 4><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 8) gather_rmsnorm_kernel<T, 8><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 14) gather_rmsnorm_kernel<T, 14><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 16) gather_rmsnorm_kernel<T, 16><<<grid, kNormThreads, 0, s>>>(a);
+  else if (vpl <= 28) gather_rmsnorm_kernel<T, 28><<<grid, kNormThreads, 0, s>>>(a);
+  else gather_rmsnorm_kernel<T, 32><<<grid, kNormThreads, 0, s>>>(a);
 }
 
 }  // namespace fdl
