@@ -349,6 +349,7 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
     wsb = _lib.attn_workspace_bytes(B, Sq, Hq, splits)
     ws = torch.empty(max(1, wsb), dtype=torch.uint8, device="cuda")
     flops = 4 * B * Hq * Sq * cap * D
+    hbm_bytes = kv_bytes + 2 * B * Sq * Hq * D * 2  # K/V + Q read + O written
     state = {"i": 0}
 
     def step():
@@ -373,7 +374,7 @@ def wl_block_attn(args, rank, world, kt: KernelTimer):
     return dict(
         metric="block attention throughput (TFLOP/s)", unit="TFLOP/s", units_per_step=flops / 1e12, step=step,
         dominant=step, graph=True, e2e_step=None, e2e_bytes=None,
-        roofline=dict(bound="tensor", per_launch=flops, kernel="block_attn_kernel", hbm_bytes=kv_bytes),
+        roofline=dict(bound="tensor", per_launch=flops, kernel="block_attn_kernel", hbm_bytes=hbm_bytes),
         launches_per_step=1 + (1 if splits > 1 else 0),
         config={"workload": "block_attn", "batch": B, "prefix": P, "q_rows": Sq, "heads": [Hq, Hkv], "splits": splits,
                 "l2": f"K/V {kv_bytes / 2**20:.0f} MiB x {nbuf} buffer sets"},
@@ -936,7 +937,7 @@ def run_kernel_suite(args, rank, world, peaks, stream):
 def e2e_dominant(breakdown, geo_B=64):
     """The largest kernel of ours in the e2e step by device time, with a
     standalone workload of the same launch shape to time it."""
-    cands = {"swiglu_kernel": "swiglu", "gather_rmsnorm_kernel": "add_rmsnorm", "block_attn_kernel": None}
+    cands = {"swiglu_kernel": "swiglu", "gather_rmsnorm_kernel": "add_rmsnorm", "block_attn_kernel": "block_attn_e2e"}
     if breakdown:
         for nm, _, _ in breakdown:
             for c, wl in cands.items():
@@ -1059,22 +1060,28 @@ def main():
     kname = None
     if w.get("stats") is not None:
         kname, wl_name = e2e_dominant(breakdown)
-        if wl_name is not None:
-            import copy
+        import copy
 
-            a2 = copy.copy(args)
-            a2.cpu_seconds = 1.0
+        a2 = copy.copy(args)
+        a2.cpu_seconds = 1.0
+        if wl_name == "block_attn_e2e":
+            # The full dKV step's attention at the bench's mean shape: 64
+            # sequences, a ~384-token sparse prefix plus the 32-key block, 32
+            # queries; HBM-bound there (176 FLOP/B, below the ridge).
+            a2.attn_b, a2.attn_p, a2.attn_sq = 64, 384, 32
+            if args.config == "e2e_1_5b":  # 1.5B geometry: 16 sequences over the full prefix
+                a2.attn_b, a2.attn_p, a2.attn_hq, a2.attn_hkv = 16, 512, 12, 2
+            wd = WORKLOADS["block_attn"](a2, rank, world, KernelTimer())
+            rf = dict(wd["roofline"])
+            rf.update(bound="hbm", per_launch=rf["hbm_bytes"], flops=wd["units_per_step"] * 1e12,
+                      kernel=f"{kname} at the e2e full-step shape (64 sequences x (384 + 32) keys, 32 queries)")
+        else:
             wd = WORKLOADS[wl_name](a2, rank, world, KernelTimer())
-            kms = launch_ms(wd["dominant"], 200, stream)
             rf = dict(wd["roofline"])
             rf["kernel"] = f"{kname} at the e2e full-block launch shape ({wd['config']['rows']} rows)"
-            traffic_key = wl_name
-            wd.clear()
-        else:
-            if rf.get("dynamic"):
-                rf["per_launch"], rf["flops"] = rf["dynamic"]()
-            kms = launch_ms(w["dominant"], 200, stream)
-            traffic_key = None
+        kms = launch_ms(wd["dominant"], 200, stream)
+        traffic_key = wl_name if args.config == "e2e_7b" else None
+        wd.clear()
     elif w.get("dominant") is not None:
         kms = launch_ms(w["dominant"], max(20, min(500, args.steps)), stream)
     else:

@@ -111,6 +111,7 @@ struct AttnParams {
   float* ws_o;
   float* ws_lse;
   int B, Sq, Hq, Hkv, G, qc, n_qchunks, cap, n_blk, mask_block, splits, n_mt;
+  int n_units;                // splits x Hkv x n_qchunks x B work items
   int kv_hmajor, blk_hmajor;  // 1: map dims are (D, S, H, B) (head-major memory)
   float scale_log2;
   int64_t o_sb, o_ss, o_sh;  // elements
@@ -118,6 +119,7 @@ struct AttnParams {
 
 struct AttnBarriers {
   uint64_t q_full;
+  uint64_t q_empty;     // the current item's S MMAs are done: Q may be reloaded
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];   // S_m(j) complete (and with it P_m(j-1) * V_(j-1))
@@ -163,6 +165,40 @@ __device__ __forceinline__ TileInfo tile_info(int i, int n1, int len, int n_blk)
   return t;
 }
 
+// One work item: a (sequence, KV head, query chunk, KV split).  Items are
+// numbered u = (b * Hkv * n_qchunks + qch * Hkv + g) * splits + split; CTA c
+// walks items c, c + gridDim.x, c + 2 * gridDim.x, ... (a persistent grid of
+// at most one CTA per SM), so the next item's Q and K/V loads and its first
+// MMAs overlap the current item's last tiles and epilogue.
+struct WorkItem {
+  int b, g, q0, split, len, n1, t_beg, T;
+};
+
+__device__ __forceinline__ WorkItem work_item(const AttnParams& p, int u, bool report_len) {
+  WorkItem w;
+  w.split = u % p.splits;
+  const int t = u / p.splits;
+  const int ny = p.Hkv * p.n_qchunks;
+  const int y = t % ny;
+  w.b = t / ny;
+  w.g = y % p.Hkv;
+  const int qch = y / p.Hkv;
+  w.q0 = qch * p.qc;
+  int len = p.seqlens[w.b];
+  if (len < 0 || len > p.cap) {
+    if (report_len && w.g == 0 && qch == 0 && w.split == 0) report(FDL_DEV_LENGTH, len);
+    len = len < 0 ? 0 : p.cap;
+  }
+  w.len = len;
+  w.n1 = (len + kBlockN - 1) / kBlockN;
+  const int n2 = p.n_blk > 0 ? (p.n_blk + kBlockN - 1) / kBlockN : 0;
+  const int n_all = w.n1 + n2;
+  const int per = (n_all + p.splits - 1) / p.splits;
+  w.t_beg = min(n_all, w.split * per);
+  w.T = min(n_all, w.t_beg + per) - w.t_beg;
+  return w;
+}
+
 // Wait without honouring the abort flag (used only to drain in-flight work).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = ptx::globaltimer();
@@ -171,35 +207,26 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// kPersistent = true: a grid of at most one CTA per SM, each walking items
+// blockIdx.x, blockIdx.x + gridDim.x, ...  false: one CTA per item (the loops
+// below then have a trip count of one the compiler can see, and compile to
+// straight-line code).
+template <bool kPersistent>
 __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
+  const int u_end = kPersistent ? p.n_units : static_cast<int>(blockIdx.x) + 1;
+  const int u_step = kPersistent ? static_cast<int>(gridDim.x) : 1;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   AttnBarriers* bars = reinterpret_cast<AttnBarriers*>(smem + kSmemBar);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
-  const int g = blockIdx.y % p.Hkv;
-  const int qch = blockIdx.y / p.Hkv;
-  const int split = blockIdx.x;
-  const int q0 = qch * p.qc;
   const int R = p.G * p.qc;
-
-  int len = p.seqlens[b];
-  if (len < 0 || len > p.cap) {
-    if (threadIdx.x == 0 && g == 0 && qch == 0 && split == 0) report(FDL_DEV_LENGTH, len);
-    len = len < 0 ? 0 : p.cap;
-  }
-  const int n1 = (len + kBlockN - 1) / kBlockN;
-  const int n2 = p.n_blk > 0 ? (p.n_blk + kBlockN - 1) / kBlockN : 0;
-  const int n_all = n1 + n2;
-  const int per = (n_all + p.splits - 1) / p.splits;
-  const int t_beg = min(n_all, split * per);
-  const int T = min(n_all, t_beg + per) - t_beg;
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(&bars->q_full, 1);
+    ptx::mbar_init(&bars->q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(&bars->kv_full[s], 1);
       ptx::mbar_init(&bars->kv_empty[s], 1);
@@ -215,7 +242,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     ptx::fence_mbar_init();
   }
   // Rows of the last MMA tile beyond R are padding: zero them so the padded
-  // MMA rows compute on finite data.
+  // MMA rows compute on finite data (no Q load ever writes them).
   {
     const int pad0 = R, pad1 = p.n_mt * 128;
     const int n16 = (pad1 - pad0) * 8;  // 16-byte chunks per half
@@ -237,64 +264,74 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
 
   if (warp == 0) {
     // ------------------------------------------------------- TMA producer
-    if (lane == 0 && T > 0) {
+    if (lane == 0) {
       ptx::prefetch_tmap(&p.tm_q);
       ptx::prefetch_tmap(&p.tm_k);
       ptx::prefetch_tmap(&p.tm_v);
-      const uint32_t qbytes = static_cast<uint32_t>(R) * 128u;
-      ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * qbytes);
-      ptx::tma_load_4d(smem + kSmemQ, &p.tm_q, &bars->q_full, 0, g * p.G, q0, b);
-      ptx::tma_load_4d(smem + kSmemQ + kQHalf, &p.tm_q, &bars->q_full, 64, g * p.G, q0, b);
-      // Tile j's coordinates in its source map.
-      auto coords = [&](int j, const CUtensorMap*& tk, const CUtensorMap*& tv, int& c1, int& c2) {
-        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
-        tk = ti.src ? &p.tm_kb : &p.tm_k;
-        tv = ti.src ? &p.tm_vb : &p.tm_v;
-        const bool hm = ti.src ? p.blk_hmajor : p.kv_hmajor;
-        c1 = hm ? ti.key0 : g;
-        c2 = hm ? g : ti.key0;
-      };
-      // L2 prefetch runs kPrefetch tiles ahead of the shared-memory loads.
-      auto prefetch = [&](int j) {
-        if (j >= T) return;
-        const CUtensorMap *tk, *tv;
-        int c1, c2;
-        coords(j, tk, tv, c1, c2);
-        ptx::tma_prefetch_l2_4d(tk, 0, c1, c2, b);
-        ptx::tma_prefetch_l2_4d(tk, 64, c1, c2, b);
-        ptx::tma_prefetch_l2_4d(tv, 0, c1, c2, b);
-        ptx::tma_prefetch_l2_4d(tv, 64, c1, c2, b);
-      };
-      for (int j = kStages; j < kStages + kPrefetch; ++j) prefetch(j);
-      int issued = 0;
-      for (int j = 0; j < T; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages) {
-          prefetch(j + kPrefetch);
-          if (!ptx::mbar_wait(&bars->kv_empty[st], ((j / kStages) - 1) & 1, abort, kWaitTimeoutNs, 1)) break;
+      int gt = 0, nq = 0, issued = 0, q_issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < u_end; u += u_step) {
+        const WorkItem it = work_item(p, u, true);
+        if (it.T == 0) continue;
+        // Q is single-buffered: the previous item's S MMAs must be done.
+        if (nq > 0) {
+          ok = ptx::mbar_wait(&bars->q_empty, (nq - 1) & 1, abort, kWaitTimeoutNs, 11);
+          if (!ok) break;
         }
-        const CUtensorMap *tk, *tv;
-        int c1, c2;
-        coords(j, tk, tv, c1, c2);
-        uint8_t* ks = smem + kSmemK + st * kKVTile;
-        uint8_t* vs = smem + kSmemV + st * kKVTile;
-        ptx::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kKVTile);
-        ptx::tma_load_4d(ks, tk, &bars->kv_full[st], 0, c1, c2, b);
-        ptx::tma_load_4d(ks + kKVHalf, tk, &bars->kv_full[st], 64, c1, c2, b);
-        ptx::tma_load_4d(vs, tv, &bars->kv_full[st], 0, c1, c2, b);
-        ptx::tma_load_4d(vs + kKVHalf, tv, &bars->kv_full[st], 64, c1, c2, b);
-        issued = j + 1;
+        const uint32_t qbytes = static_cast<uint32_t>(R) * 128u;
+        ptx::mbar_arrive_expect_tx(&bars->q_full, 2 * qbytes);
+        ptx::tma_load_4d(smem + kSmemQ, &p.tm_q, &bars->q_full, 0, it.g * p.G, it.q0, it.b);
+        ptx::tma_load_4d(smem + kSmemQ + kQHalf, &p.tm_q, &bars->q_full, 64, it.g * p.G, it.q0, it.b);
+        q_issued = nq + 1;
+        // Tile j's coordinates in its source map.
+        const int t_beg = it.t_beg, n1 = it.n1, len = it.len, g = it.g;
+        auto coords = [=, &p](int j, const CUtensorMap*& tk, const CUtensorMap*& tv, int& c1, int& c2) {
+          const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+          tk = ti.src ? &p.tm_kb : &p.tm_k;
+          tv = ti.src ? &p.tm_vb : &p.tm_v;
+          const bool hm = ti.src ? p.blk_hmajor : p.kv_hmajor;
+          c1 = hm ? ti.key0 : g;
+          c2 = hm ? g : ti.key0;
+        };
+        for (int j = 0; j < it.T; ++j, ++gt) {
+          const int st = gt % kStages;
+          // L2 prefetch of the tile that will next use this stage.
+          if (kPrefetch > 0 && j + kStages < it.T) {
+            const CUtensorMap *tk, *tv;
+            int c1, c2;
+            coords(j + kStages, tk, tv, c1, c2);
+            ptx::tma_prefetch_l2_4d(tk, 0, c1, c2, it.b);
+            ptx::tma_prefetch_l2_4d(tk, 64, c1, c2, it.b);
+            ptx::tma_prefetch_l2_4d(tv, 0, c1, c2, it.b);
+            ptx::tma_prefetch_l2_4d(tv, 64, c1, c2, it.b);
+          }
+          if (gt >= kStages) {
+            ok = ptx::mbar_wait(&bars->kv_empty[st], ((gt / kStages) - 1) & 1, abort, kWaitTimeoutNs, 1);
+            if (!ok) break;
+          }
+          const CUtensorMap *tk, *tv;
+          int c1, c2;
+          coords(j, tk, tv, c1, c2);
+          uint8_t* ks = smem + kSmemK + st * kKVTile;
+          uint8_t* vs = smem + kSmemV + st * kKVTile;
+          ptx::mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kKVTile);
+          ptx::tma_load_4d(ks, tk, &bars->kv_full[st], 0, c1, c2, it.b);
+          ptx::tma_load_4d(ks + kKVHalf, tk, &bars->kv_full[st], 64, c1, c2, it.b);
+          ptx::tma_load_4d(vs, tv, &bars->kv_full[st], 0, c1, c2, it.b);
+          ptx::tma_load_4d(vs + kKVHalf, tv, &bars->kv_full[st], 64, c1, c2, it.b);
+          issued = gt + 1;
+        }
+        ++nq;
       }
       if (*abort) {
         // Let every copy already in flight land before the CTA exits.
-        drain_wait(&bars->q_full, 0);
-        for (int j = max(0, issued - kStages); j < issued; ++j)
-          drain_wait(&bars->kv_full[j % kStages], (j / kStages) & 1);
+        if (q_issued > 0) drain_wait(&bars->q_full, (q_issued - 1) & 1);
+        for (int g = max(0, issued - kStages); g < issued; ++g) drain_wait(&bars->kv_full[g % kStages], (g / kStages) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0 && T > 0) {
+    if (lane == 0) {
       const uint32_t idesc_s = ptx::idesc_bf16_f32(128, kBlockN, false);
       const uint32_t idesc_o = ptx::idesc_bf16_f32(128, kHeadDim, true);
       // Base descriptors built once; the (16-byte-unit) address field is
@@ -302,7 +339,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       const uint64_t q_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemQ), 16, 1024);
       const uint64_t k_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemK), 16, 1024);
       const uint64_t v_desc = ptx::smem_desc_sw128(ptx::smem_u32(smem + kSmemV), kKVHalf, 1024);
-      bool issued_any = false;
       // S_m = Q_m * K_st^T: 8 MMAs of K = 16 over the 128 head dims.
       auto issue_s = [&](int m, int st) {
         const uint32_t d = tmem + kTmemS + m * kBlockN;
@@ -327,84 +363,127 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         for (int kk = 0; kk < kBlockN / 16; ++kk)
           ptx::mma_bf16_ts(d, a + kk * 8, vb + (kk * 16 * 128) / 16, idesc_o, (acc || kk > 0) ? 1u : 0u);
       };
-      bool ok = ptx::mbar_wait(&bars->q_full, 0, abort, kWaitTimeoutNs, 2) &&
-                ptx::mbar_wait(&bars->kv_full[0], 0, abort, kWaitTimeoutNs, 3);
-      if (ok) {
+      // One row tile: S in buffer buf, P in its own columns.
+      auto issue_s1 = [&](int buf, int st) {
+        const uint32_t d = tmem + kTmemS + buf * kBlockN;
+        const uint64_t kb = k_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          ptx::mma_bf16_ss(d, q_desc + ((kk >> 2) * kQHalf + (kk & 3) * 32) / 16,
+                           kb + ((kk >> 2) * kKVHalf + (kk & 3) * 32) / 16, idesc_s, kk > 0);
+      };
+      auto issue_pv1 = [&](int st, bool acc) {
+        const uint64_t vb = v_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          ptx::mma_bf16_ts(tmem + kTmemO, tmem + kTmemP1 + kk * 8, vb + (kk * 16 * 128) / 16, idesc_o,
+                           (acc || kk > 0) ? 1u : 0u);
+      };
+      // This CTA's tiles and non-empty items over all its work items: a K/V
+      // stage is released only if a later tile refills it, and q_empty is
+      // committed only if a later item reloads Q (no asynchronous arrive may
+      // still be pending when the CTA exits).
+      int total = 0, n_items = 0;
+      for (int u = blockIdx.x; u < u_end; u += u_step) {
+        const int t = work_item(p, u, false).T;
+        total += t;
+        n_items += t > 0 ? 1 : 0;
+      }
+      int gt = 0, nq = 0;
+      bool ok = true, issued_any = false;
+      for (int u = blockIdx.x; ok && u < u_end; u += u_step) {
+        const int T = work_item(p, u, false).T;
+        if (T == 0) continue;
+        const int g0 = gt;
+        const bool reload_q = nq + 1 < n_items;
+        ok = ptx::mbar_wait(&bars->q_full, nq & 1, abort, kWaitTimeoutNs, 2) &&
+             ptx::mbar_wait(&bars->kv_full[g0 % kStages], (g0 / kStages) & 1, abort, kWaitTimeoutNs, 3);
+        if (!ok) break;
         ptx::tc_fence_after();
-        for (int m = 0; m < p.n_mt; ++m) {
-          issue_s(m, 0);
-          ptx::mma_commit(&bars->s_full[m]);
-        }
-        issued_any = true;
-      }
-      if (p.n_mt == 1) {
-        // One row tile (R <= 128: sub-block rows, small GQA groups): S is
-        // double-buffered in the TMEM the second tile would use and P has its
-        // own columns, so S(j+1) is computed while the softmax works on S(j)
-        // instead of after P(j) * V_j.
-        auto issue_s1 = [&](int buf, int st) {
-          const uint32_t d = tmem + kTmemS + buf * kBlockN;
-          const uint64_t kb = k_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            ptx::mma_bf16_ss(d, q_desc + ((kk >> 2) * kQHalf + (kk & 3) * 32) / 16,
-                             kb + ((kk >> 2) * kKVHalf + (kk & 3) * 32) / 16, idesc_s, kk > 0);
-        };
-        auto issue_pv1 = [&](int st, bool acc) {
-          const uint64_t vb = v_desc + static_cast<uint64_t>(st) * (kKVTile / 16);
-#pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk)
-            ptx::mma_bf16_ts(tmem + kTmemO, tmem + kTmemP1 + kk * 8, vb + (kk * 16 * 128) / 16, idesc_o,
-                             (acc || kk > 0) ? 1u : 0u);
-        };
-        for (int j = 0; ok && j < T; ++j) {
-          const int st = j % kStages;
-          if (j + 1 < T) {
-            ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort,
-                                kWaitTimeoutNs, 4);
-            // S(j+1) reuses the buffer of S(j-1): the softmax must have read it.
-            if (ok && j >= 1)
-              ok = ptx::mbar_wait(&bars->s_free[(j + 1) & 1], ((j - 1) >> 1) & 1, abort, kWaitTimeoutNs, 5);
+        if (p.n_mt == 1) {
+          // One row tile (R <= 128: sub-block rows, small GQA groups): S is
+          // double-buffered in the TMEM the second tile would use and P has
+          // its own columns, so S(g+1) is computed while the softmax works on
+          // S(g) instead of after P(g) * V_g.  S(g) reuses the buffer of
+          // S(g-2): the softmax must have read it.
+          if (g0 >= 2) {
+            ok = ptx::mbar_wait(&bars->s_free[g0 & 1], ((g0 - 2) >> 1) & 1, abort, kWaitTimeoutNs, 5);
             if (!ok) break;
             ptx::tc_fence_after();
-            issue_s1((j + 1) & 1, (j + 1) % kStages);
-            ptx::mma_commit(&bars->s_full[(j + 1) & 1]);
           }
-          ok = ptx::mbar_wait(&bars->p_full[0], j & 1, abort, kWaitTimeoutNs, 6);
-          if (!ok) break;
-          ptx::tc_fence_after();
-          issue_pv1(st, j > 0);
-          ptx::mma_commit(&bars->pv_done[0]);
-          if (j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
-        }
-      }
-      for (int j = 0; ok && p.n_mt > 1 && j < T; ++j) {
-        const int st = j % kStages;
-        const bool nxt = j + 1 < T;
-        for (int m = 0; ok && m < p.n_mt; ++m) {
-          ok = ptx::mbar_wait(&bars->p_full[m], j & 1, abort, kWaitTimeoutNs, 6);
-          if (!ok) break;
-          ptx::tc_fence_after();
-          issue_pv(m, st, j > 0);
-          ptx::mma_commit(&bars->pv_done[m]);
-          // Stage st is free once the last row tile's P * V_j completes (only
-          // stages the producer will refill get a release; no asynchronous
-          // arrive may still be pending when the CTA exits).
-          if (m == p.n_mt - 1 && j + kStages < T) ptx::mma_commit(&bars->kv_empty[st]);
-          if (nxt) {
-            if (m == 0) {
-              ok = ptx::mbar_wait(&bars->kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort,
+          issue_s1(g0 & 1, g0 % kStages);
+          ptx::mma_commit(&bars->s_full[g0 & 1]);
+          issued_any = true;
+          if (T == 1 && reload_q) ptx::mma_commit(&bars->q_empty);
+          for (int j = 0; ok && j < T; ++j) {
+            const int g = g0 + j;
+            const int st = g % kStages;
+            if (j + 1 < T) {
+              ok = ptx::mbar_wait(&bars->kv_full[(g + 1) % kStages], ((g + 1) / kStages) & 1, abort,
                                   kWaitTimeoutNs, 4);
+              if (ok && g >= 1)
+                ok = ptx::mbar_wait(&bars->s_free[(g + 1) & 1], ((g - 1) >> 1) & 1, abort, kWaitTimeoutNs, 5);
               if (!ok) break;
+              ptx::tc_fence_after();
+              issue_s1((g + 1) & 1, (g + 1) % kStages);
+              ptx::mma_commit(&bars->s_full[(g + 1) & 1]);
+              if (j + 1 == T - 1 && reload_q) ptx::mma_commit(&bars->q_empty);
             }
-            // S_m(j+1) overwrites P_m(j): wait until P_m(j) * V_j has completed.
-            ok = ptx::mbar_wait(&bars->pv_done[m], j & 1, abort, kWaitTimeoutNs, 5);
+            ok = ptx::mbar_wait(&bars->p_full[0], g & 1, abort, kWaitTimeoutNs, 6);
             if (!ok) break;
             ptx::tc_fence_after();
-            issue_s(m, (j + 1) % kStages);
+            // The item's first P * V starts O afresh: every softmax warp read
+            // the previous item's O before it arrived on this p_full.
+            issue_pv1(st, j > 0);
+            ptx::mma_commit(&bars->pv_done[0]);
+            if (g + kStages < total) ptx::mma_commit(&bars->kv_empty[st]);
+          }
+        } else {
+          // S_m(g0) overwrites P_m(g0 - 1) of the previous item: wait until
+          // that P * V has completed.
+          for (int m = 0; ok && m < p.n_mt; ++m) {
+            if (g0 > 0) {
+              ok = ptx::mbar_wait(&bars->pv_done[m], (g0 - 1) & 1, abort, kWaitTimeoutNs, 5);
+              if (!ok) break;
+              ptx::tc_fence_after();
+            }
+            issue_s(m, g0 % kStages);
             ptx::mma_commit(&bars->s_full[m]);
+            issued_any = true;
+          }
+          if (!ok) break;
+          if (T == 1 && reload_q) ptx::mma_commit(&bars->q_empty);
+          for (int j = 0; ok && j < T; ++j) {
+            const int g = g0 + j;
+            const int st = g % kStages;
+            const bool nxt = j + 1 < T;
+            for (int m = 0; ok && m < p.n_mt; ++m) {
+              ok = ptx::mbar_wait(&bars->p_full[m], g & 1, abort, kWaitTimeoutNs, 6);
+              if (!ok) break;
+              ptx::tc_fence_after();
+              issue_pv(m, st, j > 0);
+              ptx::mma_commit(&bars->pv_done[m]);
+              // Stage st is free once the last row tile's P * V_g completes.
+              if (m == p.n_mt - 1 && g + kStages < total) ptx::mma_commit(&bars->kv_empty[st]);
+              if (nxt) {
+                if (m == 0) {
+                  ok = ptx::mbar_wait(&bars->kv_full[(g + 1) % kStages], ((g + 1) / kStages) & 1, abort,
+                                      kWaitTimeoutNs, 4);
+                  if (!ok) break;
+                }
+                // S_m(g+1) overwrites P_m(g): wait until P_m(g) * V_g has completed.
+                ok = ptx::mbar_wait(&bars->pv_done[m], g & 1, abort, kWaitTimeoutNs, 5);
+                if (!ok) break;
+                ptx::tc_fence_after();
+                issue_s(m, (g + 1) % kStages);
+                ptx::mma_commit(&bars->s_full[m]);
+                if (m == p.n_mt - 1 && j + 1 == T - 1 && reload_q) ptx::mma_commit(&bars->q_empty);
+              }
+            }
           }
         }
+        gt += T;
+        ++nq;
       }
       if (issued_any && !ok) {
         ptx::mma_commit(&bars->fin);
@@ -417,10 +496,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const int r = m * 128 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + kTmemS + m * kBlockN;
+    const uint32_t t_o = tmem + lane_off + kTmemO + m * kHeadDim;
+    int gt = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < u_end; u += u_step) {
+    const WorkItem it = work_item(p, u, false);
+    const int T = it.T;
     const int sq_i = r / p.G;
-    const int q = q0 + sq_i;
-    const int head = g * p.G + (r - sq_i * p.G);
-    const bool valid_row = (r < R) && (q < p.Sq);
+    const bool valid_row = (r < R) && (it.q0 + sq_i < p.Sq);
     // A warp whose 32 rows are all padding has nothing to compute: its P
     // lanes feed only O rows that are never stored, so it just keeps the
     // barrier phases (and leaves its SM sub-partition to the other warps).
@@ -429,35 +514,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
     // iff kp / mask_block <= qpos / mask_block, i.e. kp < kpos_end.
     int kpos_end = 0x7fffffff;
     if (p.mask_block > 0 && valid_row) {
-      const int qpos = p.q_pos ? p.q_pos[static_cast<int64_t>(b) * p.Sq + q] : len + q;
+      const int q = it.q0 + sq_i;
+      const int qpos = p.q_pos ? p.q_pos[static_cast<int64_t>(it.b) * p.Sq + q] : it.len + q;
       kpos_end = (qpos / p.mask_block + 1) * p.mask_block;
     }
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + kTmemS + m * kBlockN;
-    const uint32_t t_o = tmem + lane_off + kTmemO + m * kHeadDim;
     float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
     if (p.n_mt == 1) {
-      // Single row tile: S(j) in buffer j & 1, P in its own columns.
+      // Single row tile: S(g) in buffer g & 1, P in its own columns.
       const uint32_t t_p = tmem + lane_off + kTmemP1;
       const uint64_t sc2 = ptx::pack2(p.scale_log2, p.scale_log2);
       for (int j = 0; j < T; ++j) {
-        const int buf = j & 1;
-        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[buf], (j >> 1) & 1, abort, kWaitTimeoutNs, 7));
+        const int g = gt + j;
+        const int buf = g & 1;
+        ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[buf], (g >> 1) & 1, abort, kWaitTimeoutNs, 7));
         if (!ok) break;
         ptx::tc_fence_after();
         if (pad_warp) {
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&bars->s_free[buf]);
-          // S(j+1) may be ready long before the other warps finish P(j), so a
-          // padding warp takes its p_full turn for tile j only after
-          // P(j-1) * V_(j-1) has completed -- i.e. after every warp arrived
-          // for tile j-1.  Arriving earlier could complete phase j with this
-          // warp's arrivals for j and j+1 (an early P * V, then phases out of
+          // S(g+1) may be ready long before the other warps finish P(g), so a
+          // padding warp takes its p_full turn for tile g only after
+          // P(g-1) * V_(g-1) has completed -- i.e. after every warp arrived
+          // for tile g-1.  Arriving earlier could complete phase g with this
+          // warp's arrivals for g and g+1 (an early P * V, then phases out of
           // step).
-          if (j > 0) {
+          if (g > 0) {
             ok = __all_sync(0xffffffffu,
-                            ptx::mbar_wait(&bars->pv_done[0], (j - 1) & 1, abort, kWaitTimeoutNs, 10));
+                            ptx::mbar_wait(&bars->pv_done[0], (g - 1) & 1, abort, kWaitTimeoutNs, 10));
             if (!ok) break;
           }
           __syncwarp();
@@ -465,7 +548,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           continue;
         }
         const uint32_t t_sb = tmem + lane_off + kTmemS + buf * kBlockN;
-        const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+        const TileInfo ti = tile_info(it.t_beg + j, it.n1, it.len, p.n_blk);
         const int climit = valid_row ? max(0, min(ti.valid, kpos_end - ti.kpos0)) : kBlockN;
         const bool full = __all_sync(0xffffffffu, climit == kBlockN);
         // Max of 64 columns [c0, c0 + 64) held in lo / hi.
@@ -507,8 +590,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
           m_used = m_new;
         }
         // P and O are in use by P(j-1) * V_(j-1) until it completes.
-        if (j > 0) {
-          ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[0], (j - 1) & 1, abort, kWaitTimeoutNs, 8));
+        if (g > 0) {
+          ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[0], (g - 1) & 1, abort, kWaitTimeoutNs, 8));
           if (!ok) break;
           ptx::tc_fence_after();
         }
@@ -573,9 +656,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         if (lane == 0) ptx::mbar_arrive(&bars->p_full[0]);
       }
     }
-    for (int j = 0; p.n_mt > 1 && j < T; ++j) {
-      // S_m(j) ready (and P_m(j-1) * V_(j-1) done: O_m is stable).
-      ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], j & 1, abort, kWaitTimeoutNs, 7));
+    for (int j = 0; ok && p.n_mt > 1 && j < T; ++j) {
+      const int g = gt + j;
+      // S_m(g) ready (and P_m(g-1) * V_(g-1) done: O_m is stable).
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->s_full[m], g & 1, abort, kWaitTimeoutNs, 7));
       if (!ok) break;
       ptx::tc_fence_after();
       if (pad_warp) {
@@ -583,7 +667,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
         if (lane == 0) ptx::mbar_arrive(&bars->p_full[m]);
         continue;
       }
-      const TileInfo ti = tile_info(t_beg + j, n1, len, p.n_blk);
+      const TileInfo ti = tile_info(it.t_beg + j, it.n1, it.len, p.n_blk);
       // Visible keys of this tile for this row form a prefix of the tile.
       // Padding rows (beyond the R real rows, or past the last query) count
       // as fully visible: their results are never stored, and this keeps
@@ -706,14 +790,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars->p_full[m]);
     }
+    // The item's output coordinates, recomputed here rather than kept live
+    // through the tile loops.
+    const WorkItem ie = work_item(p, u, false);
+    const int q = ie.q0 + sq_i;
+    const int head = ie.g * p.G + (r - sq_i * p.G);
     bool have_o = ok && T > 0;
     if (have_o) {
-      have_o = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[m], (T - 1) & 1, abort, kWaitTimeoutNs, 9));
+      have_o = __all_sync(0xffffffffu, ptx::mbar_wait(&bars->pv_done[m], (gt + T - 1) & 1, abort, kWaitTimeoutNs, 9));
       ptx::tc_fence_after();
     }
     const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
     if (p.splits == 1) {
-      __nv_bfloat16* orow = p.out + b * p.o_sb + static_cast<int64_t>(q) * p.o_ss + static_cast<int64_t>(head) * p.o_sh;
+      __nv_bfloat16* orow = p.out + ie.b * p.o_sb + static_cast<int64_t>(q) * p.o_ss + static_cast<int64_t>(head) * p.o_sh;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         float o[32];
@@ -737,7 +826,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       }
     } else {
       const int64_t rows = static_cast<int64_t>(p.B) * p.Sq * p.Hq;
-      const int64_t wrow = static_cast<int64_t>(split) * rows + (static_cast<int64_t>(b) * p.Sq + q) * p.Hq + head;
+      const int64_t wrow = static_cast<int64_t>(ie.split) * rows + (static_cast<int64_t>(ie.b) * p.Sq + q) * p.Hq + head;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         float o[32];
@@ -757,6 +846,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) block_attn_kernel(const __gri
       }
       if (valid_row) p.ws_lse[wrow] = (have_o && l > 0.f) ? m_used + __log2f(l) : -INFINITY;
     }
+    gt += T;
+    }  // work items
   }
 
   ptx::tc_fence_before();

@@ -56,12 +56,25 @@ bool attn_smem_configured() {
   cudaGetDevice(&dev);
   static uint64_t mask = 0;
   if (!(mask & (1ull << dev))) {
-    if (cudaFuncSetAttribute(block_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(block_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(block_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
       return false;
     mask |= 1ull << dev;
   }
   return true;
+}
+
+// Persistent attention grid or one CTA per work item.  Measured on B200: the
+// persistent walk pays off when there are more items than SMs and each holds
+// few key tiles (the decode steps over a short sparse prefix: the next item's
+// Q and K/V loads and first MMAs hide the current item's tail and epilogue);
+// with long items the per-CTA set-up is already amortised and the one-item
+// form is faster.
+constexpr int kPersistMaxTiles = 8;
+bool attn_persistent(int64_t units, int tiles_per_unit) {
+  return units > num_sms() && tiles_per_unit <= kPersistMaxTiles;
 }
 
 // Split-KV count for `work_items` (batch x KV head x query chunk) CTAs of
@@ -482,7 +495,6 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
   p.qc = sq < 256 / G ? sq : 256 / G;
   p.n_qchunks = (sq + p.qc - 1) / p.qc;
   p.n_mt = (G * p.qc + 127) / 128;
-  if (p.n_qchunks * hkv > 65535) return FDL_E_SHAPE;
   int splits = num_splits > 0 ? num_splits : fdl_block_attn_auto_splits(batch, sq, hq, hkv, cap, n_blk);
   if (splits > 1) {
     const int64_t need = fdl_block_attn_workspace_bytes(batch, sq, hq, head_dim, splits);
@@ -521,6 +533,9 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
   p.B = batch; p.Sq = sq; p.Hq = hq; p.Hkv = hkv; p.cap = cap; p.n_blk = n_blk;
   p.mask_block = mask_block;
   p.splits = splits;
+  const int64_t units = static_cast<int64_t>(splits) * hkv * p.n_qchunks * batch;
+  if (units >= (1ll << 31)) return FDL_E_SHAPE;
+  p.n_units = static_cast<int>(units);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.o_sb = o_sb; p.o_ss = o_ss; p.o_sh = o_sh;
   const int64_t rows = static_cast<int64_t>(batch) * sq * hq;
@@ -529,7 +544,14 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
     p.ws_lse = p.ws_o + static_cast<int64_t>(splits) * rows * head_dim;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  block_attn_kernel<<<dim3(splits, hkv * p.n_qchunks, batch), kAttnThreads, kSmemBytes, s>>>(p);
+  const int tiles_all = (cap + kBlockN - 1) / kBlockN + (n_blk + kBlockN - 1) / kBlockN;
+  if (attn_persistent(units, (tiles_all + splits - 1) / splits)) {
+    // One CTA per SM (the kernel's shared memory allows no more), each
+    // walking its share of the work items.
+    block_attn_kernel<true><<<num_sms(), kAttnThreads, kSmemBytes, s>>>(p);
+  } else {
+    block_attn_kernel<false><<<static_cast<unsigned>(units), kAttnThreads, kSmemBytes, s>>>(p);
+  }
   int rc = launch_status();
   if (rc != FDL_OK || splits == 1) return rc;
   attn_combine_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(p.ws_o, p.ws_lse, p.out, splits, batch,

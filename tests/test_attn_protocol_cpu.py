@@ -218,6 +218,209 @@ def two_row_tiles(seed, T, pad_tile1, tma):
     return ok, sim.errors
 
 
+# ---------------------------------------------------------------------------
+# Persistent form: one CTA walks several work items (sequence x KV head x
+# query chunk x split) with per-CTA running tile counters, so every per-tile
+# barrier keeps its phase sequence across items.  Per item: the producer
+# reloads Q only after the previous item's last S MMA (q_empty, a commit);
+# the issuer waits q_full before the item's first S; the softmax warps do the
+# item's epilogue (read O after its last P*V) before they take part in the
+# next item's tiles, which is what lets the next item's first P*V (the one
+# that overwrites O) follow from p_full alone.  Items may hold no tiles.
+# ---------------------------------------------------------------------------
+
+
+def _persistent_producer(sim, units):
+    gt = nq = 0
+    for T in units:
+        if T == 0:
+            continue
+        if nq > 0:
+            yield from sim.wait("q_empty", (nq - 1) & 1)
+        if sim.state.get("S_in_flight")():
+            sim.errors.append(f"Q of item {nq} loaded while an S MMA of the previous item is in flight")
+        yield from sim.delay(*sim.tma)
+        sim.bars["q_full"].arrive()
+        for _ in range(T):
+            st = gt % 2
+            if gt >= 2:
+                yield from sim.wait(f"kv_empty{st}", ((gt // 2) - 1) & 1)
+            yield from sim.delay(*sim.tma)
+            sim.bars[f"kv_full{st}"].arrive()
+            gt += 1
+        nq += 1
+
+
+def persistent_two_row_tiles(seed, units, pad_tile1, tma):
+    sim = _Sim(seed, tma)
+    for name, c in [("kv_full0", 1), ("kv_full1", 1), ("kv_empty0", 1), ("kv_empty1", 1), ("s_full0", 1),
+                    ("s_full1", 1), ("p_full0", 4), ("p_full1", 4), ("pv_done0", 1), ("pv_done1", 1),
+                    ("q_full", 1), ("q_empty", 1)]:
+        sim.bar(name, c)
+    total = sum(units)
+    wrote, o_read = set(), set()
+    sim.state["S_in_flight"] = lambda: any(k == "S" for _, k, *_ in sim.pending)
+
+    def pad(m, w):
+        return m == 1 and w >= 4 - pad_tile1
+
+    def issuer():
+        gt = nq = 0
+        for T in units:
+            if T == 0:
+                continue
+            g0 = gt
+            yield from sim.wait("q_full", nq & 1)
+            yield from sim.wait(f"kv_full{g0 % 2}", (g0 // 2) & 1)
+            for m in range(2):
+                if g0 > 0:
+                    yield from sim.wait(f"pv_done{m}", (g0 - 1) & 1)
+                sim.mma("S", g0, m)
+                sim.commit(f"s_full{m}")
+            if T == 1:
+                sim.commit("q_empty")
+            for j in range(T):
+                g = g0 + j
+                for m in range(2):
+                    yield from sim.wait(f"p_full{m}", g & 1)
+                    if any((m, g, w) not in wrote for w in range(4) if not pad(m, w)):
+                        sim.errors.append(f"P*V{m}({g}) issued before every computing warp wrote P")
+                    if j == 0 and nq > 0 and any((nq - 1, m, w) not in o_read for w in range(4)):
+                        sim.errors.append(f"first P*V{m} of item {nq} overwrites O before the epilogue read it")
+                    sim.mma("PV", g, m)
+                    sim.commit(f"pv_done{m}")
+                    if m == 1 and g + 2 < total:
+                        sim.commit(f"kv_empty{g % 2}")
+                    if j + 1 < T:
+                        if m == 0:
+                            yield from sim.wait(f"kv_full{(g + 1) % 2}", ((g + 1) // 2) & 1)
+                        yield from sim.wait(f"pv_done{m}", g & 1)
+                        if not sim.complete("PV", g, m):
+                            sim.errors.append(f"S{m}({g + 1}) over P{m}({g}) while P*V reads it")
+                        sim.mma("S", g + 1, m)
+                        sim.commit(f"s_full{m}")
+                        if m == 1 and j + 1 == T - 1:
+                            sim.commit("q_empty")
+            gt += T
+            nq += 1
+
+    def softmax(m, w):
+        gt = nq = 0
+        for T in units:
+            if T == 0:
+                continue
+            for j in range(T):
+                g = gt + j
+                yield from sim.wait(f"s_full{m}", g & 1)
+                if pad(m, w):
+                    sim.bars[f"p_full{m}"].arrive()
+                    continue
+                if j > 0 and not sim.complete("PV", g - 1, m):
+                    sim.errors.append("O rescaled while P*V is in flight")
+                yield from sim.delay(5, 40)
+                wrote.add((m, g, w))
+                sim.bars[f"p_full{m}"].arrive()
+            yield from sim.wait(f"pv_done{m}", (gt + T - 1) & 1)  # epilogue: O of this item
+            if not sim.complete("PV", gt + T - 1, m):
+                sim.errors.append("epilogue read O before the item's last P*V completed")
+            yield from sim.delay(2, 15)
+            o_read.add((nq, m, w))
+            gt += T
+            nq += 1
+
+    progs = [_persistent_producer(sim, units), issuer()] + [softmax(m, w) for m in range(2) for w in range(4)]
+    ok = sim.run(progs)
+    return ok, sim.errors
+
+
+def persistent_one_row_tile(seed, units, n_pad, tma):
+    sim = _Sim(seed, tma)
+    for name, c in [("kv_full0", 1), ("kv_full1", 1), ("kv_empty0", 1), ("kv_empty1", 1), ("s_full0", 1),
+                    ("s_full1", 1), ("p_full", 4), ("pv_done", 1), ("s_free0", 4), ("s_free1", 4),
+                    ("q_full", 1), ("q_empty", 1)]:
+        sim.bar(name, c)
+    total = sum(units)
+    wrote, read, o_read = set(), set(), set()
+    sim.state["S_in_flight"] = lambda: any(k == "S" for _, k, *_ in sim.pending)
+
+    def issue_s(g):
+        if g >= 2:
+            yield from sim.wait(f"s_free{g & 1}", ((g - 2) >> 1) & 1)
+            if any((g - 2, w) not in read for w in range(4)):
+                sim.errors.append(f"S({g}) overwrites S({g - 2}) before every warp read it")
+        sim.mma("S", g, 0)
+        sim.commit(f"s_full{g & 1}")
+
+    def issuer():
+        gt = nq = 0
+        for T in units:
+            if T == 0:
+                continue
+            g0 = gt
+            yield from sim.wait("q_full", nq & 1)
+            yield from sim.wait(f"kv_full{g0 % 2}", (g0 // 2) & 1)
+            yield from issue_s(g0)
+            if T == 1:
+                sim.commit("q_empty")
+            for j in range(T):
+                g = g0 + j
+                if j + 1 < T:
+                    yield from sim.wait(f"kv_full{(g + 1) % 2}", ((g + 1) // 2) & 1)
+                    yield from issue_s(g + 1)
+                    if j + 1 == T - 1:
+                        sim.commit("q_empty")
+                yield from sim.wait("p_full", g & 1)
+                if any((g, w) not in wrote for w in range(4 - n_pad)):
+                    sim.errors.append(f"P*V({g}) issued before every computing warp wrote P({g})")
+                if j == 0 and nq > 0 and any((nq - 1, w) not in o_read for w in range(4)):
+                    sim.errors.append(f"first P*V of item {nq} overwrites O before the epilogue read it")
+                sim.mma("PV", g, 0)
+                sim.commit("pv_done")
+                if g + 2 < total:
+                    sim.commit(f"kv_empty{g % 2}")
+            gt += T
+            nq += 1
+
+    def softmax(w):
+        pad = w >= 4 - n_pad
+        gt = nq = 0
+        for T in units:
+            if T == 0:
+                continue
+            for j in range(T):
+                g = gt + j
+                buf = g & 1
+                yield from sim.wait(f"s_full{buf}", (g >> 1) & 1)
+                if pad:
+                    read.add((g, w))
+                    sim.bars[f"s_free{buf}"].arrive()
+                    if g > 0:
+                        yield from sim.wait("pv_done", (g - 1) & 1)
+                    sim.bars["p_full"].arrive()
+                    continue
+                yield from sim.delay(3, 20)
+                if g > 0:
+                    yield from sim.wait("pv_done", (g - 1) & 1)  # P (and, within the item, O) free
+                    if not sim.complete("PV", g - 1, 0):
+                        sim.errors.append("P rewritten while P*V is in flight")
+                yield from sim.delay(3, 20)
+                read.add((g, w))
+                sim.bars[f"s_free{buf}"].arrive()
+                yield from sim.delay(3, 20)
+                wrote.add((g, w))
+                sim.bars["p_full"].arrive()
+            yield from sim.wait("pv_done", (gt + T - 1) & 1)
+            if not sim.complete("PV", gt + T - 1, 0):
+                sim.errors.append("epilogue read O before the item's last P*V completed")
+            yield from sim.delay(2, 15)
+            o_read.add((nq, w))
+            gt += T
+            nq += 1
+
+    ok = sim.run([_persistent_producer(sim, units), issuer()] + [softmax(w) for w in range(4)])
+    return ok, sim.errors
+
+
 TMA = [(1, 4), (1, 30), (60, 150)]  # K/V tiles from L2 at once ... slow HBM loads
 
 
@@ -248,3 +451,26 @@ def test_padding_warps_need_their_turn():
         ok, errors = one_row_tile(seed, 5, 2, (1, 4), gate_padding=False)
         broken += (not ok) or bool(errors)
     assert broken > 0
+
+
+UNITS = [[3], [1, 1], [2, 0, 3], [1, 4, 2], [0, 2, 1, 1], [5, 5], [1, 0, 0, 1]]
+
+
+@pytest.mark.parametrize("tma", TMA)
+def test_persistent_two_row_tiles_protocol(tma):
+    for units in UNITS:
+        for pad_tile1 in (0, 2):
+            for seed in range(15):
+                ok, errors = persistent_two_row_tiles(seed, units, pad_tile1, tma)
+                assert ok, f"wait that never finishes: items={units} pad={pad_tile1} seed={seed}"
+                assert not errors, (units, pad_tile1, seed, errors[:3])
+
+
+@pytest.mark.parametrize("tma", TMA)
+def test_persistent_one_row_tile_protocol(tma):
+    for units in UNITS:
+        for n_pad in (0, 2):
+            for seed in range(15):
+                ok, errors = persistent_one_row_tile(seed, units, n_pad, tma)
+                assert ok, f"wait that never finishes: items={units} pad={n_pad} seed={seed}"
+                assert not errors, (units, n_pad, seed, errors[:3])
