@@ -7,19 +7,14 @@
 // the chosen token (generation_functions.py:2290-2291), without materialising
 // the [rows, V] probabilities or running a separate softmax, max and gather.
 //
-// One CTA per row, one read of the row:
+// One CTA per row, two passes over the row:
 //   1. per thread an online (max, sum) over its 16-byte vectors (a rescale
 //      only when the thread's max grows), merged by a fixed xor-butterfly and
-//      a fixed shared-memory tree -- the same sum on every run.  Only entries
-//      within 1/64 of the row max m can round to p_max (exp(-1/64) / s is
-//      more than a bf16 ulp below 1 / s), so each thread also keeps, in
-//      index order, up to kSampleCands entries within 1/64 of its own running
-//      max: an entry below its thread's running max - 1/64 is below m - 1/64
-//      too, so no entry that can tie is dropped;
-//   2. each thread tests its kept entries -- the probability formed exactly
-//      as defined above -- and the smallest index equal to p_max wins; a
-//      thread that had more entries in its window than it could keep reads
-//      its part of the row again.
+//      a fixed shared-memory tree -- the same sum on every run;
+//   2. the row again (L2-resident right after pass 1): only entries within
+//      1/64 of m can round to p_max (exp(-1/64) / s is more than a bf16 ulp
+//      below 1 / s), and for those the probability is formed exactly as in
+//      pass 1's definition; the smallest index that equals p_max wins.
 #pragma once
 #include "common.cuh"
 
@@ -28,7 +23,6 @@ namespace fdl {
 constexpr int kSampleThreads = 512;
 constexpr int kSampleWarps = kSampleThreads / 32;
 constexpr float kSampleTieWindow = 1.0f / 64.0f;
-constexpr int kSampleCands = 4;  // entries near the running max kept per thread
 
 struct SampleArgs {
   const __nv_bfloat16* logits;  // [rows, V] with row stride rs (elements)
@@ -54,52 +48,31 @@ __global__ void __launch_bounds__(kSampleThreads) softmax_argmax_kernel(const __
   const int row = blockIdx.x;
   const __nv_bfloat16* x = a.logits + static_cast<int64_t>(row) * a.rs;
   const int nvec = a.V / 8;  // whole 16-byte vectors; the tail is handled per element
-  // ---- pass 1: online max and sum of exp, and the entries near the max
+  // ---- pass 1: online max and sum of exp
   float m = -INFINITY, s = 0.f;
-  int c_idx[kSampleCands];
-  float c_val[kSampleCands];
-  int nc = 0;
-  bool overflow = false;
-  auto visit = [&](float l, int v) {
+  for (int i = threadIdx.x; i < nvec; i += kSampleThreads) {
+    const uint4 u = ld_stream16(reinterpret_cast<const char*>(x) + static_cast<int64_t>(i) * 16);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+    float vmax = __bfloat162float(e[0]);
+#pragma unroll
+    for (int k = 1; k < 8; ++k) vmax = fmaxf(vmax, __bfloat162float(e[k]));
+    if (vmax > m) {
+      s = (m == -INFINITY) ? 0.f : s * expf(m - vmax);
+      m = vmax;
+    }
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += expf(__bfloat162float(e[k]) - m);
+    }
+  }
+  for (int v = nvec * 8 + threadIdx.x; v < a.V; v += kSampleThreads) {
+    const float l = __bfloat162float(x[v]);
     if (l > m) {
       s = (m == -INFINITY) ? 0.f : s * expf(m - l);
-      if (l > m + kSampleTieWindow) {  // every kept entry fell out of the window
-        nc = 0;
-        overflow = false;
-      }
       m = l;
     }
     if (m != -INFINITY) s += expf(l - m);
-    if (l >= m - kSampleTieWindow) {
-#pragma unroll
-      for (int c = 0; c < kSampleCands; ++c)
-        if (c == nc) {
-          c_idx[c] = v;
-          c_val[c] = l;
-        }
-      overflow |= nc == kSampleCands;
-      nc += nc < kSampleCands ? 1 : 0;
-    }
-  };
-  constexpr int kU = 4;  // vectors in flight per thread
-  for (int i0 = threadIdx.x; i0 < nvec; i0 += kU * kSampleThreads) {
-    uint4 u[kU];
-#pragma unroll
-    for (int k = 0; k < kU; ++k) {
-      const int i = i0 + k * kSampleThreads;
-      if (i < nvec) u[k] = ld_stream16(reinterpret_cast<const char*>(x) + static_cast<int64_t>(i) * 16);
-    }
-#pragma unroll
-    for (int k = 0; k < kU; ++k) {
-      const int i = i0 + k * kSampleThreads;
-      if (i < nvec) {
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[k]);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) visit(__bfloat162float(e[t]), i * 8 + t);
-      }
-    }
   }
-  for (int v = nvec * 8 + threadIdx.x; v < a.V; v += kSampleThreads) visit(__bfloat162float(x[v]), v);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
@@ -128,26 +101,25 @@ __global__ void __launch_bounds__(kSampleThreads) softmax_argmax_kernel(const __
   __syncthreads();
   const float M = sh_row[0], S = sh_row[1];
   const __nv_bfloat16 pmax = __float2bfloat16_rn(expf(0.f) / S);
-  const float lo = M - kSampleTieWindow;
-  auto ties = [&](float l) {
-    return l >= lo && __bfloat16_as_ushort(__float2bfloat16_rn(expf(l - M) / S)) == __bfloat16_as_ushort(pmax);
-  };
   // ---- pass 2: first index whose rounded probability equals pmax
   int best = 0x7fffffff;
-  if (!overflow) {
+  const float lo = M - kSampleTieWindow;
+  for (int i = threadIdx.x; i < nvec; i += kSampleThreads) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<int64_t>(i) * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-    for (int c = kSampleCands - 1; c >= 0; --c)  // kept in index order: the last hit is the smallest
-      if (c < nc && ties(c_val[c])) best = c_idx[c];
-  } else {
-    for (int i = threadIdx.x; i < nvec; i += kSampleThreads) {
-      const uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<int64_t>(i) * 8);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (i * 8 + k < best && ties(__bfloat162float(e[k]))) best = i * 8 + k;
+    for (int k = 0; k < 8; ++k) {
+      const float l = __bfloat162float(e[k]);
+      if (l >= lo && i * 8 + k < best &&
+          __bfloat16_as_ushort(__float2bfloat16_rn(expf(l - M) / S)) == __bfloat16_as_ushort(pmax))
+        best = i * 8 + k;
     }
-    for (int v = nvec * 8 + threadIdx.x; v < a.V; v += kSampleThreads)
-      if (v < best && ties(__bfloat162float(x[v]))) best = v;
+  }
+  for (int v = nvec * 8 + threadIdx.x; v < a.V; v += kSampleThreads) {
+    const float l = __bfloat162float(x[v]);
+    if (l >= lo && v < best &&
+        __bfloat16_as_ushort(__float2bfloat16_rn(expf(l - M) / S)) == __bfloat16_as_ushort(pmax))
+      best = v;
   }
   if (best != 0x7fffffff) atomicMin(&sh_idx, best);
   __syncthreads();
