@@ -319,3 +319,36 @@ def test_compaction_at_decode_size_and_refused_orders():
     torch.ops.fdl.kv_compact([buf], torch.tensor([1, 0], device=DEV))
     assert torch.equal(buf, keep)
     assert _lib.last_device_error() == (1, 0)  # FDL_DEV_INDEX, active[1] = 0 < 1
+
+
+def test_seqused_masks_match_the_reference_semantics_and_attention():
+    """get_seqused_mask / get_seqused_mask_batched (utils/static_kv_cache.py:
+    286-302): an additive [B, 1, 1, max_S] mask, 0 for key j < the valid
+    length and -inf beyond, written into one persistent buffer (the same
+    tensor every call, so a captured graph sees the refill).  SDPA under the
+    batched mask equals the library's flash_kvcache over the same lengths, as
+    the reference's SDPA fallback relies on."""
+    B, S, L, H, D = 3, 160, 1, 4, 128
+    cache = StaticKVCache(B, S, L, H, D, torch.bfloat16, DEV)
+    m1 = cache.get_seqused_mask(37)
+    ref = np.zeros((B, 1, 1, S), np.float32)
+    ref[..., 37:] = -np.inf
+    assert m1.shape == (B, 1, 1, S) and np.array_equal(m1.float().cpu().numpy(), ref)
+    seqused = torch.tensor([5, 160, 64], dtype=torch.int32, device=DEV)
+    m2 = cache.get_seqused_mask_batched(seqused)
+    assert m2.data_ptr() == m1.data_ptr()
+    ref = np.zeros((B, 1, 1, S), np.float32)
+    for b, n in enumerate([5, 160, 64]):
+        ref[b, ..., n:] = -np.inf
+    assert np.array_equal(m2.float().cpu().numpy(), ref)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    q = (torch.randn(B, 32, H * 7, D, generator=g, device=DEV) / D ** 0.5).to(torch.bfloat16)
+    k = torch.randn(B, S, H, D, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, S, H, D, generator=g, device=DEV).to(torch.bfloat16)
+    kk = k.transpose(1, 2).repeat_interleave(7, dim=1).float()
+    vv = v.transpose(1, 2).repeat_interleave(7, dim=1).float()
+    sdpa = torch.nn.functional.scaled_dot_product_attention(q.transpose(1, 2).float(), kk, vv,
+                                                            attn_mask=m2.float()).transpose(1, 2)
+    out = get_attention_backend().flash_kvcache_attention(q, k, v, seqused)
+    assert_close("flash_kvcache vs SDPA under the seqused mask", out.float().cpu().numpy(),
+                 sdpa.cpu().numpy(), ATOL, RTOL)
