@@ -1035,6 +1035,15 @@ def main():
                     "seconds": fms / 1e3, "includes": "prompt prefill + every 32-token block of the generation"}
         _fdl_lib.check_device("bench full generation")
 
+    # Sequence-sharded output: one all-gather of every rank's whole generated
+    # sequences (prompt + all blocks of the generation just timed), the only
+    # collective besides the max-time reductions.
+    collected = None
+    if world > 1 and w.get("collect"):
+        from fast_v2_b200.sharding import gather_generated
+
+        collected = list(gather_generated(w["collect"](), pad_id=-1).shape)
+
     # Roofline of the dominant kernel.  Kernel-level configs: the config's own
     # kernel.  e2e configs: the largest kernel of this library in the step by
     # device time (attribution from one untimed, traced block), timed alone at
@@ -1094,15 +1103,6 @@ def main():
                 break
         roof["step_breakdown"] = dom_shares
 
-    # Sequence-sharded output: one all-gather of every rank's generated
-    # sequences after the timed regions (the only collective besides the
-    # max-time reduction).
-    collected = None
-    if world > 1 and w.get("collect"):
-        from fast_v2_b200.sharding import gather_generated
-
-        collected = list(gather_generated(w["collect"](), pad_id=-1).shape)
-
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
@@ -1128,7 +1128,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": meta["dtype"], "data": "synthetic",
             "config": {**meta["config"], "parallelism": f"dp{world} (sequence-sharded replicas)",
-                       **({"gathered": collected} if collected else {})},
+                       **({"gathered_sequences": collected} if collected else {})},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": (meta["launches_per_step"] * args.steps
                              if meta["launches_per_step"] is not None else launches_timed),

@@ -212,3 +212,36 @@ def test_packed_gather_rejects_an_inconsistent_cu_seqlens():
     code, info = _lib.last_device_error()
     assert code == 1 and info == 2
     assert float(ok[150:].float().abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("Sq,n_blk,splits", [(32, 32, 0), (13, 32, 0), (8, 0, 0), (32, 0, 2)])
+def test_block_attn_persistent_items_with_empty_and_tiny_sequences(Sq, n_blk, splits):
+    """More work items than SMs with a few key tiles each puts the kernel on
+    its persistent path (one CTA per SM walking several items).  Sequences of
+    length 0 (items with no prefix tiles, or none at all without a block),
+    length 1 and lengths straddling tile boundaries are mixed so consecutive
+    items of one CTA differ in tile count; with splits=2 items of one sequence
+    land on different CTAs and go through the combine."""
+    B, cap = 96, 512
+    g = torch.Generator(device=DEV).manual_seed(6000 + Sq + n_blk + splits)
+    lens = torch.tensor([[0, 1, 127, 128, 129, 300, 511, 512][i % 8] for i in range(B)], dtype=torch.int32)
+    q = (torch.randn(B, Sq, HQ, D, generator=g, device=DEV) / math.sqrt(D)).to(torch.bfloat16)
+    k = torch.randn(B, cap, HKV, D, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, cap, HKV, D, generator=g, device=DEV).to(torch.bfloat16)
+    kb = vb = None
+    if n_blk:
+        kb = torch.randn(B, HKV, n_blk, D, generator=g, device=DEV).to(torch.bfloat16).transpose(1, 2)
+        vb = torch.randn(B, HKV, n_blk, D, generator=g, device=DEV).to(torch.bfloat16).transpose(1, 2)
+    ns = splits or _lib.attn_auto_splits(B, Sq, HQ, HKV, cap, n_blk)
+    wsb = _lib.attn_workspace_bytes(B, Sq, HQ, ns)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV) if wsb > 0 else None
+    out = torch.full_like(q, 7.0)
+    torch.ops.fdl.block_attn(q, k, v, lens.to(DEV), kb, vb, None, 0, D ** -0.5, out, ws, ns)
+    for b in range(0, B, 5):
+        L = int(lens[b])
+        ref = O.block_attention(q[b:b + 1].float().cpu().numpy(), k[b:b + 1, :max(L, 1)].float().cpu().numpy(),
+                                v[b:b + 1, :max(L, 1)].float().cpu().numpy(), [L],
+                                k_blk=None if kb is None else kb[b:b + 1].float().cpu().numpy(),
+                                v_blk=None if vb is None else vb[b:b + 1].float().cpu().numpy())
+        assert_close(f"persistent Sq={Sq} blk={n_blk} splits={ns} b={b} L={L}", out[b:b + 1].float().cpu().numpy(),
+                     ref, ATOL, RTOL)
