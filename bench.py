@@ -21,7 +21,8 @@ Configs (BASELINE.json `configs`):
                 random init, 64 sequences/GPU, prompt 1024, dKV block cache
                 + token-sparse prefix; one step = one 32-token block
   e2e_1_5b      the same at Qwen2.5-1.5B geometry, 16 sequences, prompt 256,
-                static cache (full block recompute every step)
+                static cache (batch_sample_dynamo's schedule: full-block
+                forward every step, block K/V as scratch rows of the cache)
 
 Inputs are seeded synthetic tensors (the reference's datasets and weights are
 not available offline).  Between timed steps the inputs rotate through buffer
@@ -404,11 +405,12 @@ def _e2e(args, rank, world, kt, geo_name):
     from fast_v2_b200.block_decode import QWEN25_1_5B, QWEN25_7B, BlockDiffusionDecoder, BlockDiffusionLM, param_count
 
     if geo_name == "7b":
-        geo, B, P, G, sparse, refresh = QWEN25_7B, 64, 1024, 1024, 0.25, 4
+        geo, B, P, G, sparse, refresh, schedule = QWEN25_7B, 64, 1024, 1024, 0.25, 4, "dkv"
         cache_desc = "dynamic block KV (dKV, refresh 4) + token-sparse prefix (top 25% by key norm, per block)"
     else:
-        geo, B, P, G, sparse, refresh = QWEN25_1_5B, 16, 256, 512, None, 1
-        cache_desc = "static KV cache, full block recompute every step"
+        geo, B, P, G, sparse, refresh, schedule = QWEN25_1_5B, 16, 256, 512, None, 1, "static"
+        cache_desc = ("static KV cache (batch_sample_dynamo schedule): a full-block forward every step, the "
+                      "block's K/V written as scratch rows of the cache, unmasked attention over cache[:len + 32]")
     B = args.e2e_batch or B
     # The decode capacity covers every block of the run (warm-up + timed + two
     # spare); G (the configured generation length) is the minimum.
@@ -437,7 +439,8 @@ def _e2e(args, rank, world, kt, geo_name):
                 "l2": "weights and KV cache stream from HBM every forward (>> L2)"})
     dec = None if cpu_only else BlockDiffusionDecoder(model, B, P, G, refresh=refresh, sparse_keep=sparse,
                                                       fed_bucket=getattr(args, "fed_bucket", 1), use_graphs=True,
-                                                      fused_kv_store=getattr(args, "kv_store", "fused") == "fused")
+                                                      fused_kv_store=getattr(args, "kv_store", "fused") == "fused",
+                                                      schedule=schedule)
     if not cpu_only:
         # One seeded global batch of B x world prompts; each rank decodes its
         # own contiguous shard of sequences (sequence_shard), as the
@@ -1083,7 +1086,8 @@ def main():
             wd = WORKLOADS["block_attn"](a2, rank, world, KernelTimer())
             rf = dict(wd["roofline"])
             rf.update(bound="hbm", per_launch=rf["hbm_bytes"], flops=wd["units_per_step"] * 1e12,
-                      kernel=f"{kname} at the e2e full-step shape (64 sequences x (384 + 32) keys, 32 queries)")
+                      kernel=f"{kname} at the e2e full-step shape ({a2.attn_b} sequences x ({a2.attn_p} + 32) keys, "
+                             f"32 queries)")
         else:
             wd = WORKLOADS[wl_name](a2, rank, world, KernelTimer())
             rf = dict(wd["roofline"])

@@ -26,6 +26,11 @@ The decode loop follows the reference's dKV sampler ``batch_sample_dkv``
 * block complete: commit forward over the 32 final tokens appends their K/V
   to the committed cache; its last logit gives the next bridge token.
 
+The static-cache sampler ``batch_sample_dynamo`` (generation_functions.py:
+243-900, the static-cache configuration) is the ``schedule="static"`` of the
+same decoder: full-block steps only, the block's K/V written as scratch rows
+of the committed cache, unmasked attention over cache[:lens + T].
+
 ``sparse_keep`` (a keep fraction, e.g. 0.25) replaces the committed prefix
 seen by the diffusion steps with the top-scoring prefix tokens by key norm,
 re-selected once per block (no reference counterpart; see
@@ -225,11 +230,13 @@ class DecodeState:
         self.attn_ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev) if wsb > 0 else None
 
     # -------------------------------------------------------------- pieces
-    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos, lens=None):
+    def attend(self, q, l, prefix: str, k_blk, v_blk, q_pos, lens=None, mask_block=None):
         """Block attention for layer l: queries q [B, T, Hq, D] over the
         committed prefix ("full": the first `lens` rows of the cache, default
         self.lens) or the sparse prefix ("sparse") followed by the given block
-        K/V (none when k_blk is None), under the block-causal mask."""
+        K/V (none when k_blk is None), under the block-causal mask of
+        `mask_block` positions (default the block size; 0 = every key
+        visible)."""
         g = self.model.geo
         out = torch.empty_like(q)
         if prefix == "sparse":
@@ -243,7 +250,8 @@ class DecodeState:
         ws = self.attn_ws
         if ns > 1 and (ws is None or ws.numel() < _lib.attn_workspace_bytes(self.B, T, g.heads, ns)):
             ws = torch.empty(_lib.attn_workspace_bytes(self.B, T, g.heads, ns), dtype=torch.uint8, device=q.device)
-        torch.ops.fdl.block_attn(q, kp, vp, lens, k_blk, v_blk, q_pos, self.block, g.head_dim ** -0.5, out,
+        mb = self.block if mask_block is None else mask_block
+        torch.ops.fdl.block_attn(q, kp, vp, lens, k_blk, v_blk, q_pos, mb, g.head_dim ** -0.5, out,
                                  ws if ns > 1 else None, ns)
         _lib.count_launches(2 if ns > 1 else 1)
         return out
@@ -257,12 +265,13 @@ class DecodeState:
             _lib.count_launches(3)
 
     # ------------------------------------------------------------ forwards
-    def forward_commit(self, ids, pos, all_rows: bool = False):
+    def forward_commit(self, ids, pos, all_rows: bool = False, mask_block=None):
         """Forward over a fully decoded span (prompt prefill or a finished
         block) that appends its K/V to the committed cache at self.lens and
-        attends over committed prefix + span (block-causal).  Returns the
-        final-normed hidden state of the span's last row [B, hidden] (all rows
-        [B, T, hidden] with all_rows=True)."""
+        attends over committed prefix + span (block-causal; mask_block=0: the
+        static-cache sampler's unmasked attention over cache[:lens + T]).
+        Returns the final-normed hidden state of the span's last row
+        [B, hidden] (all rows [B, T, hidden] with all_rows=True)."""
         m = self.model
         B, T = ids.shape
         h = F.embedding(ids, m.embed)
@@ -277,9 +286,9 @@ class DecodeState:
         def attend_layer(l, layer, x):
             if self.fused_kv_store:
                 q = m.qkv_into(layer, x, pos, self.k[l], self.v[l], start=self.lens)
-                return self.attend(q, l, "full", None, None, qpos, lens=lens_after)
+                return self.attend(q, l, "full", None, None, qpos, lens=lens_after, mask_block=mask_block)
             q, k, v = m.qkv(layer, x, pos)
-            a = self.attend(q, l, "full", k, v, qpos)
+            a = self.attend(q, l, "full", k, v, qpos, mask_block=mask_block)
             torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
             _lib.count_launches(1)
             return a
@@ -289,6 +298,34 @@ class DecodeState:
         if all_rows:
             return m.rmsnorm(h, m.norm)
         return m.rmsnorm(h[:, -1:].contiguous(), m.norm)[:, 0]
+
+    def forward_scratch(self, ids, pos):
+        """Diffusion step of the static-cache sampler (batch_sample_dynamo,
+        generation_functions.py:754-775, and the patched attention forward,
+        utils/attention_backends.py:873-898): the block's K/V are written as
+        scratch rows at the committed length (``write_scratch_compiled`` at
+        ``kv_write_start``) and every query attends over cache[:lens + T]
+        with no mask (``scratch_seqlens``, ``is_causal=False``).  The committed
+        length does not move; the next step overwrites the same rows and the
+        commit forward rewrites them with the final tokens.  Returns the
+        last-layer hidden state [B, T, hidden] (before the final norm)."""
+        m = self.model
+        B, T = ids.shape
+        h = F.embedding(ids, m.embed)
+        pos = pos.contiguous()
+        qpos = pos.to(torch.int32).contiguous()
+        lens_after = self.lens + T
+
+        def attend_layer(l, layer, x):
+            if self.fused_kv_store:
+                q = m.qkv_into(layer, x, pos, self.k[l], self.v[l], start=self.lens)
+            else:
+                q, k, v = m.qkv(layer, x, pos)
+                torch.ops.fdl.kv_append([self.k[l]], [self.v[l]], [k], [v], self.lens)
+                _lib.count_launches(1)
+            return self.attend(q, l, "full", None, None, qpos, lens=lens_after, mask_block=0)
+
+        return m.layers_forward(h, attend_layer)
 
     def forward_block(self, ids, pos, fed=None, seed_hidden=None, prefix="full"):
         """dKV diffusion step over the current block (forward_dkv,
@@ -351,7 +388,12 @@ def dkv_fed_indices(prv_transfer_idx: torch.Tensor, width: int | None = None):
 
 class BlockDiffusionDecoder:
     """Greedy (temperature 0) block-diffusion decode of a batch with the dKV
-    schedule of batch_sample_dkv (generation_functions.py:2132-2340).
+    schedule of batch_sample_dkv (generation_functions.py:2132-2340), or with
+    ``schedule="static"`` the static-cache schedule of batch_sample_dynamo
+    (generation_functions.py:243-900, no block cache): every diffusion step
+    is a full-block forward whose K/V are scratch rows of the committed cache
+    (DecodeState.forward_scratch), and prefill, steps and commit attend with
+    no mask over cache[:lens + T].
 
     Every diffusion step works on static device buffers (block tokens,
     positions, sub-block index, frozen masks, seed hidden states), so with
@@ -363,8 +405,17 @@ class BlockDiffusionDecoder:
     def __init__(self, model: BlockDiffusionLM, batch: int, prompt_len: int, gen_len: int, block: int = 32,
                  sub_block: int = 8, threshold: float = 0.9, refresh: int = 4, sparse_keep: float | None = None,
                  fed_bucket: int = 1, mask_id: int = MASK_ID, stop_id: int = STOP_ID, pad_id: int = PAD_ID,
-                 use_graphs: bool = False, fused_kv_store: bool = True):
+                 use_graphs: bool = False, fused_kv_store: bool = True, schedule: str = "dkv"):
         assert prompt_len % block == 0 and block % sub_block == 0
+        if schedule not in ("dkv", "static"):
+            raise ValueError(f"schedule must be 'dkv' or 'static', not {schedule!r}")
+        if schedule == "static" and sparse_keep:
+            raise ValueError("the static-cache schedule attends over the whole committed cache (no sparse prefix)")
+        self.schedule = schedule
+        # The static-cache sampler attends with no mask over cache[:lens + T]
+        # in every forward, the prefill included; the dKV sampler's prefill
+        # and commit are block-causal.
+        self.commit_mask = 0 if schedule == "static" else None
         self.m, self.B, self.block, self.sub = model, batch, block, sub_block
         self.threshold, self.refresh, self.fed_bucket = threshold, refresh, fed_bucket
         self.mask_id, self.stop_id, self.pad_id = mask_id, stop_id, pad_id
@@ -430,6 +481,9 @@ class BlockDiffusionDecoder:
         self.status[1] = (~self.prv).sum(1).max()
 
     def _full_step(self):
+        if self.schedule == "static":
+            self._sample(self.st.forward_scratch(self.x, self.pos))
+            return
         h = self.st.forward_block(self.x, self.pos, prefix=self.prefix)
         self.seed.copy_(h)
         self._sample(self.seed)
@@ -454,7 +508,7 @@ class BlockDiffusionDecoder:
 
     def _commit_step(self):
         """Commit the decoded block to the KV cache; next bridge token."""
-        hl = self.st.forward_commit(self.x, self.pos)
+        hl = self.st.forward_commit(self.x, self.pos, mask_block=self.commit_mask)
         nxt = self.m.logits_rows(hl).argmax(-1, keepdim=True)
         nxt.masked_fill_(self.finished[:, None], self.pad_id)
         self.nxt.copy_(nxt)
@@ -501,7 +555,8 @@ class BlockDiffusionDecoder:
         """Capture every step variant up front (full step and cached widths)."""
         if not self.use_graphs:
             return
-        for key in ["begin", "full", "commit"] + list(range(self.fed_bucket, self.block + 1, self.fed_bucket)):
+        widths = [] if self.schedule == "static" else list(range(self.fed_bucket, self.block + 1, self.fed_bucket))
+        for key in ["begin", "full", "commit"] + widths:
             if key not in self._graphs:
                 self._capture(key)
         _lib.check_device("BlockDiffusionDecoder.capture_all")
@@ -521,7 +576,7 @@ class BlockDiffusionDecoder:
         pos = torch.arange(P, device=prompt.device).unsqueeze(0).expand(B, -1)
         self.st.lens.zero_()
         self.finished.zero_()
-        hl = self.st.forward_commit(prompt, pos)
+        hl = self.st.forward_commit(prompt, pos, mask_block=self.commit_mask)
         bridge = self.m.logits_rows(hl).argmax(-1, keepdim=True)
         _lib.check_device("BlockDiffusionDecoder.prefill")
         return bridge
@@ -546,7 +601,7 @@ class BlockDiffusionDecoder:
                 # never ends); fail loudly instead of spinning.
                 if n_fwd >= 4 * blk:
                     raise RuntimeError("block decode made no progress: the model keeps predicting the mask token")
-                if step_in_block <= 1 or step_in_block % self.refresh == 0:
+                if self.schedule == "static" or step_in_block <= 1 or step_in_block % self.refresh == 0:
                     self._run("full")
                 else:
                     self._run(min(blk, max(1, -(-fed_n // self.fed_bucket) * self.fed_bucket)))
