@@ -8,11 +8,13 @@ parity; MMA completion reaches a barrier through a commit that fires when
 every MMA issued before it has finished.  Timing decides which interleavings
 happen on the GPU, and the GPU tests see only a few of them.  The model
 replays the protocol of both pipelines -- one row tile (S double-buffered, P
-in its own TMEM columns) and two row tiles (P over S, S(j+1) after P(j)*V_j)
--- with random latencies, from K/V tiles that arrive at once (L2-resident)
+in its own TMEM columns) and two row tiles (P over S, S(j+1) queued right
+behind P(j)*V_j: the tensor core runs one thread's MMAs in issue order, as the
+model does) -- with random latencies, from K/V tiles that arrive at once (L2-resident)
 to slow ones, and checks: no wait that can never finish, every P*V_j issued
 only after each computing warp wrote P(j), no S buffer rewritten before every
-warp read it, and O rescaled only after the previous P*V completed.
+warp read it (nor before the P*V that reads P out of it has finished), and O
+rescaled only after the previous P*V completed.
 
 It also shows why the padding warps of the one-tile pipeline take their
 p_full turn only after P(j-1)*V_(j-1): without that gate, fast K/V tiles let
@@ -49,6 +51,9 @@ class _Sim:
         self.next_id = 0
         self.errors = []
         self.state = {}
+        self.ids = {}
+        self.start = {}
+        self.finish = {}
 
     def bar(self, name, count):
         self.bars[name] = _Bar(count)
@@ -57,9 +62,16 @@ class _Sim:
         i = self.next_id
         self.next_id += 1
         start = max([f for f, *_ in self.pending] + [self.now])
-        self.pending.append((start + self.rnd.randint(5, 20), kind, j, m, i))
+        fin = start + self.rnd.randint(5, 20)
+        self.pending.append((fin, kind, j, m, i))
         self.issued.append(i)
+        self.ids[(kind, j, m)] = i
+        self.start[i], self.finish[i] = start, fin
         return i
+
+    def runs_after(self, i, kind, j, m):
+        """MMA i starts only once the MMA (kind, j, m) has finished."""
+        return self.finish[self.ids[(kind, j, m)]] <= self.start[i]
 
     def complete(self, kind, j, m):
         return not any(k == kind and jj == j and mm == m for _, k, jj, mm, _ in self.pending)
@@ -167,8 +179,8 @@ def one_row_tile(seed, T, n_pad, tma, gate_padding=True):
 
 
 def two_row_tiles(seed, T, pad_tile1, tma):
-    """n_mt == 2: P_m(j) over S_m(j); S_m(j+1) issued after P_m(j)*V_j; the
-    last pad_tile1 warps of row tile 1 hold only padding rows."""
+    """n_mt == 2: P_m(j) over S_m(j); S_m(j+1) queued right behind P_m(j)*V_j;
+    the last pad_tile1 warps of row tile 1 hold only padding rows."""
     sim = _Sim(seed, tma)
     for name, c in [("kv_full0", 1), ("kv_full1", 1), ("kv_empty0", 1), ("kv_empty1", 1), ("s_full0", 1),
                     ("s_full1", 1), ("p_full0", 4), ("p_full1", 4), ("pv_done0", 1), ("pv_done1", 1)]:
@@ -195,10 +207,9 @@ def two_row_tiles(seed, T, pad_tile1, tma):
                 if j + 1 < T:
                     if m == 0:
                         yield from sim.wait(f"kv_full{(j + 1) % 2}", ((j + 1) // 2) & 1)
-                    yield from sim.wait(f"pv_done{m}", j & 1)
-                    if not sim.complete("PV", j, m):
+                    i = sim.mma("S", j + 1, m)
+                    if not sim.runs_after(i, "PV", j, m):
                         sim.errors.append(f"S{m}({j + 1}) over P{m}({j}) while P*V reads it")
-                    sim.mma("S", j + 1, m)
                     sim.commit(f"s_full{m}")
 
     def softmax(m, w):
@@ -294,10 +305,9 @@ def persistent_two_row_tiles(seed, units, pad_tile1, tma):
                     if j + 1 < T:
                         if m == 0:
                             yield from sim.wait(f"kv_full{(g + 1) % 2}", ((g + 1) // 2) & 1)
-                        yield from sim.wait(f"pv_done{m}", g & 1)
-                        if not sim.complete("PV", g, m):
+                        i = sim.mma("S", g + 1, m)
+                        if not sim.runs_after(i, "PV", g, m):
                             sim.errors.append(f"S{m}({g + 1}) over P{m}({g}) while P*V reads it")
-                        sim.mma("S", g + 1, m)
                         sim.commit(f"s_full{m}")
                         if m == 1 and j + 1 == T - 1:
                             sim.commit("q_empty")
