@@ -99,6 +99,50 @@ int pick_splits(int work_items, int tiles_est) {
   return best;
 }
 
+// Query chunk of one CTA: the G query heads of a KV head times qc queries
+// form the CTA's MMA rows, at most max_rows of them, in equal chunks.
+int attn_qc_for(int sq, int G, int max_rows) {
+  const int cap_q = std::max(1, max_rows / G);
+  const int nq = (sq + cap_q - 1) / cap_q;
+  return (sq + nq - 1) / nq;
+}
+
+struct AttnPlan {
+  int qc, splits;
+};
+
+// Chunking and split-KV count of one launch.  Up to 256 rows per CTA (two
+// 128-row tiles, P over S) or up to 128 (one row tile: S double-buffered, P in
+// its own columns -- half the rows per key tile, but twice the CTAs for the
+// same work and no split-KV combine where the 256-row form needs one to fill
+// the GPU).  The choice is an estimate in microseconds fitted to B200
+// measurements of both forms (batch 1-64, prefix 512-8192, 32 queries, 7 query
+// heads per KV head): per CTA about 9 us of fixed cost plus 2.18 us per key
+// tile with two row tiles or 1.72 us with one, times the waves of CTAs over
+// the SMs; a split adds about 6 us plus the fp32 partial rows written and read
+// back by the combine pass.
+AttnPlan plan_attn(int batch, int sq, int G, int hkv, int tiles, int forced_splits) {
+  const int sms = num_sms();
+  AttnPlan best{attn_qc_for(sq, G, 256), 1};
+  double best_us = 1e300;
+  for (int max_rows : {256, 128}) {
+    const int qc = attn_qc_for(sq, G, max_rows);
+    if (max_rows == 128 && qc == best.qc) break;  // one chunking only
+    const int64_t units = static_cast<int64_t>(batch) * hkv * ((sq + qc - 1) / qc);
+    const int s = forced_splits > 0 ? forced_splits
+                                    : pick_splits(static_cast<int>(std::min<int64_t>(units, INT32_MAX)), tiles);
+    const int64_t waves = (units * s + sms - 1) / sms;
+    const int per = (tiles + s - 1) / s;
+    double us = static_cast<double>(waves) * (9.0 + per * (G * qc > 128 ? 2.18 : 1.72));
+    if (s > 1) us += 6.0 + static_cast<double>(batch) * sq * G * hkv * s * 1024.0 / 6.0e6;
+    if (us < best_us) {
+      best_us = us;
+      best = {qc, s};
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 extern "C" {
@@ -461,10 +505,8 @@ int fdl_block_attn_auto_splits(int batch, int sq, int hq, int hkv, int cap, int 
   if (batch < 1 || sq < 1 || hq < 1 || hkv < 1 || hq % hkv) return 1;
   const int G = hq / hkv;
   if (G > 256) return 1;
-  const int qc = sq < 256 / G ? sq : 256 / G;
-  const int nq = (sq + qc - 1) / qc;
   const int tiles = (cap + kBlockN - 1) / kBlockN + (n_blk + kBlockN - 1) / kBlockN;
-  return pick_splits(batch * hkv * nq, tiles);
+  return plan_attn(batch, sq, G, hkv, tiles, 0).splits;
 }
 
 int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* seqlens, int cap, const void* k_blk,
@@ -492,10 +534,12 @@ int fdl_block_attn(const void* q, const void* k, const void* v, const int32_t* s
   if (q_sh > q_ss && sq > 1) return FDL_E_UNSUPPORTED;  // query memory must be [B, S, H, D]
   AttnParams p{};
   p.G = G;
-  p.qc = sq < 256 / G ? sq : 256 / G;
+  const AttnPlan plan = plan_attn(batch, sq, G, hkv,
+                                  (cap + kBlockN - 1) / kBlockN + (n_blk + kBlockN - 1) / kBlockN, num_splits);
+  p.qc = plan.qc;
   p.n_qchunks = (sq + p.qc - 1) / p.qc;
   p.n_mt = (G * p.qc + 127) / 128;
-  int splits = num_splits > 0 ? num_splits : fdl_block_attn_auto_splits(batch, sq, hq, hkv, cap, n_blk);
+  int splits = plan.splits;
   if (splits > 1) {
     const int64_t need = fdl_block_attn_workspace_bytes(batch, sq, hq, head_dim, splits);
     if (!workspace || workspace_bytes < need) {
