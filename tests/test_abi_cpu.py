@@ -34,6 +34,10 @@ def test_host_side_argument_checks_without_gpu():
     assert _lib.attn_workspace_bytes(2, 32, 28, 4) >= 4 * 2 * 32 * 28 * 129 * 4
     assert _lib.attn_auto_splits(64, 32, 28, 4, 8224, 0) == 1
     assert _lib.attn_auto_splits(1, 32, 28, 4, 8224, 0) > 1
+    # B=16 at a short prefix runs as 128-row CTAs (two 16-query chunks) with
+    # no split; at P=8192 it keeps the 256-row form with two KV splits.
+    assert _lib.attn_auto_splits(16, 32, 28, 4, 544, 0) == 1
+    assert _lib.attn_auto_splits(16, 32, 28, 4, 8224, 0) == 2
 
 
 def test_torch_ops_meta_shapes():

@@ -70,6 +70,39 @@ def test_block_attn_config3_grid(B, P, Sq):
         assert_close(f"B={B} P={P} Sq={Sq} splits={ns} b={b}", out[b:b + 1].float().cpu().numpy(), ref, ATOL, RTOL)
 
 
+@pytest.mark.parametrize("splits", [0, 1])
+@pytest.mark.parametrize("mask", [0, 32])
+def test_block_attn_config4_geometry(mask, splits):
+    """Config 4's attention (Qwen2.5-1.5B: 12 query heads over 2 KV heads, 16
+    sequences, 32 queries over cache[:len + 32] with ragged lengths), without
+    the static schedule's mask (mask 0) and with the block-causal one (queries
+    at positions len..len+31).  The library's own choice (splits 0) runs
+    256-row CTAs (6 heads x 32 queries = 192 rows) with four KV splits; with
+    one split it runs 128-row CTAs (6 x 16 = 96 rows: one row tile with a
+    whole padding warp)."""
+    B, Sq, Hq, Hkv = 16, 32, 12, 2
+    g = torch.Generator(device=DEV).manual_seed(3400 + mask)
+    lens = torch.randint(200, 800, (B,), generator=g, device=DEV)
+    cap = int(lens.max()) + 32 + 64
+    q = (torch.randn(B, Sq, Hq, D, generator=g, device=DEV) / math.sqrt(D)).to(torch.bfloat16)
+    k = torch.randn(B, cap, Hkv, D, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, cap, Hkv, D, generator=g, device=DEV).to(torch.bfloat16)
+    seq = (lens + 32).to(torch.int32)
+    q_pos = (lens[:, None] + torch.arange(Sq, device=DEV)[None, :]).to(torch.int32).contiguous()
+    ns = splits or _lib.attn_auto_splits(B, Sq, Hq, Hkv, cap, 0)
+    wsb = _lib.attn_workspace_bytes(B, Sq, Hq, ns)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV) if wsb > 0 else None
+    out = torch.empty_like(q)
+    torch.ops.fdl.block_attn(q, k, v, seq, None, None, q_pos if mask else None, mask, D ** -0.5, out, ws, ns)
+    for b in _sample(B):
+        n = int(seq[b])
+        qp = q_pos[b].cpu().numpy() if mask else None
+        ref = O.block_attention(q[b:b + 1].float().cpu().numpy(), k[b:b + 1, :n].float().cpu().numpy(),
+                                v[b:b + 1, :n].float().cpu().numpy(), [n],
+                                **({"q_pos": qp[None, :], "mask_block": mask} if mask else {}))
+        assert_close(f"config4 mask={mask} splits={ns} b={b}", out[b:b + 1].float().cpu().numpy(), ref, ATOL, RTOL)
+
+
 @pytest.mark.parametrize("B,P", [(16, 8192), (64, 2048)])
 def test_block_attn_config3_ragged_lengths(B, P):
     """Same grid points with per-sequence lengths drawn from [1, P+32] (partial
