@@ -77,28 +77,6 @@ bool attn_persistent(int64_t units, int tiles_per_unit) {
   return units > num_sms() && tiles_per_unit <= kPersistMaxTiles;
 }
 
-// Split-KV count for `work_items` (batch x KV head x query chunk) CTAs of
-// about `tiles_est` key tiles each.  Cost model in key-tile times: waves x
-// (per-CTA fixed cost of about 2 tiles -- Q load, TMEM and barrier setup,
-// pipeline fill, epilogue -- plus the CTA's share of the tiles), plus about one
-// tile for the combine pass when split.  One CTA per SM.
-int pick_splits(int work_items, int tiles_est) {
-  const int sms = num_sms();
-  const int max_s = std::min(64, std::max(1, tiles_est));
-  int best = 1;
-  int64_t best_cost = INT64_MAX;
-  for (int s = 1; s <= max_s; ++s) {
-    const int64_t waves = (static_cast<int64_t>(work_items) * s + sms - 1) / sms;
-    const int64_t per = (tiles_est + s - 1) / s;
-    const int64_t cost = waves * (2 + per) + (s > 1 ? 1 : 0);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
-}
-
 // Query chunk of one CTA: the G query heads of a KV head times qc queries
 // form the CTA's MMA rows, at most max_rows of them, in equal chunks.
 int attn_qc_for(int sq, int G, int max_rows) {
@@ -115,29 +93,36 @@ struct AttnPlan {
 // 128-row tiles, P over S) or up to 128 (one row tile: S double-buffered, P in
 // its own columns -- half the rows per key tile, but twice the CTAs for the
 // same work and no split-KV combine where the 256-row form needs one to fill
-// the GPU).  The choice is an estimate in microseconds fitted to B200
-// measurements of both forms (batch 1-64, prefix 512-8192, 32 queries, 7 query
-// heads per KV head): per CTA about 9 us of fixed cost plus 2.18 us per key
-// tile with two row tiles or 1.72 us with one, times the waves of CTAs over
-// the SMs; a split adds about 6 us plus the fp32 partial rows written and read
-// back by the combine pass.
+// the GPU).  Both forms and every split count are scored by an estimate in
+// microseconds fitted to B200 measurements of both forms (batch 1-64, prefix
+// 256-8192, 32 queries, 6 and 7 query heads per KV head): per CTA about 9 us
+// of fixed cost plus 2.18 us per key tile with two row tiles or 1.72 us with
+// one, times the waves of CTAs over the SMs; a split adds about 6 us plus the
+// fp32 partial rows written and read back by the combine pass.  A forced split
+// count (num_splits > 0) is kept; only the chunking is chosen then.
 AttnPlan plan_attn(int batch, int sq, int G, int hkv, int tiles, int forced_splits) {
   const int sms = num_sms();
-  AttnPlan best{attn_qc_for(sq, G, 256), 1};
+  AttnPlan best{attn_qc_for(sq, G, 256), forced_splits > 0 ? forced_splits : 1};
   double best_us = 1e300;
+  const int max_s = std::min(64, std::max(1, tiles));
+  int prev_qc = 0;
   for (int max_rows : {256, 128}) {
     const int qc = attn_qc_for(sq, G, max_rows);
-    if (max_rows == 128 && qc == best.qc) break;  // one chunking only
+    if (qc == prev_qc) break;  // one chunking only
+    prev_qc = qc;
     const int64_t units = static_cast<int64_t>(batch) * hkv * ((sq + qc - 1) / qc);
-    const int s = forced_splits > 0 ? forced_splits
-                                    : pick_splits(static_cast<int>(std::min<int64_t>(units, INT32_MAX)), tiles);
-    const int64_t waves = (units * s + sms - 1) / sms;
-    const int per = (tiles + s - 1) / s;
-    double us = static_cast<double>(waves) * (9.0 + per * (G * qc > 128 ? 2.18 : 1.72));
-    if (s > 1) us += 6.0 + static_cast<double>(batch) * sq * G * hkv * s * 1024.0 / 6.0e6;
-    if (us < best_us) {
-      best_us = us;
-      best = {qc, s};
+    const double t_tile = G * qc > 128 ? 2.18 : 1.72;
+    const int s_lo = forced_splits > 0 ? forced_splits : 1;
+    const int s_hi = forced_splits > 0 ? forced_splits : max_s;
+    for (int s = s_lo; s <= s_hi; ++s) {
+      const int64_t waves = (units * s + sms - 1) / sms;
+      const int per = (tiles + s - 1) / s;
+      double us = static_cast<double>(waves) * (9.0 + per * t_tile);
+      if (s > 1) us += 6.0 + static_cast<double>(batch) * sq * G * hkv * s * 1024.0 / 6.0e6;
+      if (us < best_us) {
+        best_us = us;
+        best = {qc, s};
+      }
     }
   }
   return best;

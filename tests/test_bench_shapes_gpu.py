@@ -70,16 +70,17 @@ def test_block_attn_config3_grid(B, P, Sq):
         assert_close(f"B={B} P={P} Sq={Sq} splits={ns} b={b}", out[b:b + 1].float().cpu().numpy(), ref, ATOL, RTOL)
 
 
-@pytest.mark.parametrize("splits", [0, 1])
+@pytest.mark.parametrize("splits", [0, 4])
 @pytest.mark.parametrize("mask", [0, 32])
 def test_block_attn_config4_geometry(mask, splits):
     """Config 4's attention (Qwen2.5-1.5B: 12 query heads over 2 KV heads, 16
     sequences, 32 queries over cache[:len + 32] with ragged lengths), without
     the static schedule's mask (mask 0) and with the block-causal one (queries
     at positions len..len+31).  The library's own choice (splits 0) runs
-    256-row CTAs (6 heads x 32 queries = 192 rows) with four KV splits; with
-    one split it runs 128-row CTAs (6 x 16 = 96 rows: one row tile with a
-    whole padding warp)."""
+    128-row CTAs (6 heads x 16 queries = 96 rows: one row tile with a whole
+    padding warp) without a split; with four splits forced it runs 256-row
+    CTAs (6 x 32 = 192 rows, the second row tile half padding) and the
+    combine pass."""
     B, Sq, Hq, Hkv = 16, 32, 12, 2
     g = torch.Generator(device=DEV).manual_seed(3400 + mask)
     lens = torch.randint(200, 800, (B,), generator=g, device=DEV)
