@@ -38,6 +38,10 @@ def test_host_side_argument_checks_without_gpu():
     # no split; at P=8192 it keeps the 256-row form with two KV splits.
     assert _lib.attn_auto_splits(16, 32, 28, 4, 544, 0) == 1
     assert _lib.attn_auto_splits(16, 32, 28, 4, 8224, 0) == 2
+    # config 4's geometry (12 query / 2 KV heads): one pass of 96-row CTAs
+    # at short prefixes, where splitting 192-row CTAs measured 20-34% slower
+    assert _lib.attn_auto_splits(16, 32, 12, 2, 288, 0) == 1
+    assert _lib.attn_auto_splits(16, 32, 12, 2, 544, 0) == 1
 
 
 def test_torch_ops_meta_shapes():
