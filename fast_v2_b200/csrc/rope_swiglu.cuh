@@ -184,28 +184,23 @@ struct SwigluArgs {
 // x / (1 + exp(-x)) with IEEE division, rounded to bf16.
 __device__ __forceinline__ float silu_bf16_exact(float x) { return bf16r(__fdiv_rn(x, __fadd_rn(1.f, expf(-x)))); }
 
-// Same value, mostly from the special-function unit: s = x * rcp(1 + 2^(-x
-// log2 e)) is within a few fp32 ulps of the IEEE expression, so it rounds to
-// the same bf16 unless it lies within kSiluGuard ulps of a rounding midpoint
-// (low 16 bits near 0x8000); those inputs, and non-finite or subnormal ones,
-// take the exact expression.  The gate is a bf16 value, so the result is
-// checked exhaustively over all 65536 gate values against torch's silu (the
-// fast expression alone already matches on all of them; the guard keeps a
-// margin at a cost of about 5% of the kernel time).
-#ifndef FDL_SILU_GUARD
-#define FDL_SILU_GUARD 16
-#endif
-constexpr int kSiluGuard = FDL_SILU_GUARD;
-__device__ __forceinline__ float silu_bf16(float x) {
+// Same value from the special-function unit: s = x * rcp(1 + 2^(-x log2 e)).
+// For every bf16 gate value it rounds to the same bf16 as the IEEE
+// expression except for x in (-88.7, -87.3), where 1 + 2^(-x log2 e) is so
+// large that its flush-to-zero reciprocal is 0 (gate values -87.5, -88 and
+// -88.5 give -0 instead of about -5e-37); inputs below -87 take the exact
+// expression.  The kernel only sees bf16 gate values, and the GPU tests check
+// all 65536 of them against torch's bf16 silu.  (An earlier guard on the
+// result -- within 16 fp32 ulps of a bf16 rounding midpoint, or not normal --
+// cost 11% of the kernel time for the same outputs.)
+__device__ __forceinline__ float silu_bf16_fast(float x) {
   float e, r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.44269504f));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
-  const float s = x * r;
-  const uint32_t bits = __float_as_uint(s);
-  const int low = static_cast<int>(bits & 0xFFFFu) - 0x8000;
-  const bool finite = (bits & 0x7F800000u) != 0x7F800000u && (bits & 0x7F800000u) != 0u;
-  if (__builtin_expect(!finite || (low < kSiluGuard && low > -kSiluGuard), 0)) return silu_bf16_exact(x);
-  return bf16r(s);
+  return bf16r(x * r);
+}
+__device__ __forceinline__ float silu_bf16(float x) {
+  return x < -87.f ? silu_bf16_exact(x) : silu_bf16_fast(x);
 }
 
 // The rows x (F / 8) vectors of the output form one flat range and every
@@ -231,9 +226,18 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const __grid_con
   const __nv_bfloat16* u = reinterpret_cast<const __nv_bfloat16*>(&uu);
   uint4 o;
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(&o);
+  float gf[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e)
-    y[e] = __float2bfloat16_rn(__fmul_rn(silu_bf16(__bfloat162float(g[e])), __bfloat162float(u[e])));
+  for (int e = 0; e < 8; ++e) gf[e] = __bfloat162float(g[e]);
+  // One test per vector: the exact expression is needed only below -87.
+  const float lo = fminf(fminf(fminf(gf[0], gf[1]), fminf(gf[2], gf[3])), fminf(fminf(gf[4], gf[5]), fminf(gf[6], gf[7])));
+  if (__builtin_expect(lo < -87.f, 0)) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = __float2bfloat16_rn(__fmul_rn(silu_bf16(gf[e]), __bfloat162float(u[e])));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = __float2bfloat16_rn(__fmul_rn(silu_bf16_fast(gf[e]), __bfloat162float(u[e])));
+  }
   *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(r) * a.out_rs + v * 8) = o;
 }
 

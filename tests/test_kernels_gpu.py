@@ -411,8 +411,10 @@ def test_swiglu_matches_reference_rounding():
 
 
 def test_swiglu_exhaustive_gate_values():
-    """The fast silu path with its rounding-midpoint guard gives torch's
-    bf16 silu for every one of the 65536 bf16 gate values (up = 1)."""
+    """The kernel's silu (special-function ex2 and rcp, the exact expression
+    only for gates below -87, where the flush-to-zero reciprocal underflows)
+    gives torch's bf16 silu for every one of the 65536 bf16 gate values
+    (up = 1)."""
     F_ = 65536
     gate = torch.arange(F_, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
     gu = torch.cat([gate, torch.ones(F_, dtype=torch.bfloat16)]).view(1, 2 * F_).to(DEV)
